@@ -1,0 +1,561 @@
+"""Benchmark driver for the B200 GEMM hot path.
+
+Default (driver contract):  python bench.py [--gpus N] [--steps K] [--warmup W]
+  One process per GPU (torchrun for N > 1). The headline workload is BASELINE
+  a16w16 FP16 C = A @ B^T with M = 4096, K = 8192 and 4096 columns of
+  C per GPU - B is sharded along N across the ranks (A replicated, no collective
+  in the timed loop), so per-GPU work is fixed as N grows ("weak" scaling).
+  The same line carries the BF8 and MXFP4 rates at
+  the same shape, a roofline object for the GEMM kernel, the CPU baseline, an
+  end-to-end number through the public API with host buffers, the clocks seen
+  while timing and (N > 1) a separately timed NCCL all-gather of the C slabs.
+
+  --impl reference   times the reference's CPU path for the same workload
+                     (torch.matmul in fp16 on the host cores - the oracle's
+                     restatement of kernels/gemm/intra_wave/a16w16/bench.py:183).
+  --config large     BASELINE configs[4]: MXFP4 16384 x 53248 x 16384 with N
+                     split over the ranks (fixed total work: "strong" scaling).
+
+Reference bench surface (kernels/gemm/intra_wave/<kind>/bench.py:133-164):
+  python bench.py --kernel a16w16|a8w8|a4w4 [--K 8192] [--dtype fp16 bf16]
+                  [--M 4096 --N 4096] [--rocprof] [--rotating-buffer-size 512]
+  runs the correctness check against torch on the GPU and prints the TFLOPS
+  table, or with --rocprof 1000 launches over rotating buffers for an external
+  profiler (ncu here).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
+TRAFFIC_PATH = os.path.join(ROOT, "profiles", "traffic.json")
+METRIC = "GEMM TFLOPS/GPU & % of dtype dense peak (FP16, BF8, MXFP4) at 1/2/4/8 B200"
+NOMINAL_DENSE_TFLOPS = {"fp16": 2250.0, "bf16": 2250.0, "bf8": 4500.0, "mxfp4": 9000.0}
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+# ----------------------------------------------------------------- helpers --
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def load_peaks() -> tuple[dict, str]:
+    try:
+        with open(PEAKS_PATH) as f:
+            return json.load(f), "measured"
+    except (OSError, ValueError):
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+def tensor_peak(dtype_name: str, peaks: dict) -> float:
+    """Dense peak for a dtype: the measured bf16 GEMM rate scaled by the
+    hardware's dtype ratio (fp8 2x, fp4 4x of fp16/bf16)."""
+    mult = {"fp16": 1.0, "bf16": 1.0, "bf8": 2.0, "mxfp4": 4.0}[dtype_name]
+    return peaks["bf16_tflops"] * mult
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons while timing."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
+        sm, smax, reasons, power = [], [], set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "power_w_max": max(power) if power else None,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group(
+            "nccl", timeout=datetime.timedelta(seconds=120),
+            device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    if world != n_gpus and rank == 0:
+        log(f"note: --gpus {n_gpus} but WORLD_SIZE={world}; using {world}")
+    return rank, world, local
+
+
+def barrier(world: int):
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+# --------------------------------------------------------------- workloads --
+class Workload:
+    """One GEMM configuration with rotating device inputs (cold L2 per step)."""
+
+    def __init__(self, name: str, M: int, N: int, K: int, dtype_name: str, sets: int,
+                 seed: int):
+        from gfx950_gluon_tutorials_b200 import ops
+        self.ops = ops
+        self.name, self.M, self.N, self.K, self.dtype_name = name, M, N, K, dtype_name
+        self.flops = 2.0 * M * N * K
+        dev = torch.device("cuda", torch.cuda.current_device())
+        gen = torch.Generator(device=dev).manual_seed(seed)
+        self.sets = []
+        for _ in range(sets):
+            self.sets.append(self._make(gen, dev))
+        self.launches_per_step = 1 if dtype_name in ("fp16", "bf16") else 3
+
+    def _make(self, gen, dev):
+        M, N, K = self.M, self.N, self.K
+        if self.dtype_name in ("fp16", "bf16"):
+            dt = torch.float16 if self.dtype_name == "fp16" else torch.bfloat16
+            a = (torch.randn((M, K), generator=gen, device=dev) / K ** 0.5).to(dt)
+            b = (torch.randn((N, K), generator=gen, device=dev) / K ** 0.5).to(dt)
+            return {"a": a, "b": b, "c": torch.empty((M, N), dtype=dt, device=dev)}
+        if self.dtype_name == "bf8":
+            out = {}
+            for key, rows in (("a", M), ("b", N)):
+                x = torch.randn((rows, K), generator=gen, device=dev)
+                e = torch.randint(125, 130, (rows, K // 32), generator=gen, device=dev).to(
+                    torch.uint8)
+                out[key] = self.ops.quantize_mxe5m2(x, e)
+                out["s" + key] = e
+                del x
+            out["c"] = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+            return out
+        out = {}
+        for key, rows in (("a", M), ("b", N)):
+            x = torch.randn((rows, K), generator=gen, device=dev)
+            rows_pad = (rows + 255) // 256 * 256
+            out[key], out["s" + key] = self.ops.quantize_mxfp4(x, rows_pad=rows_pad)
+            del x
+        out["c"] = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+        return out
+
+    def run(self, i: int):
+        s = self.sets[i % len(self.sets)]
+        if self.dtype_name in ("fp16", "bf16"):
+            return self.ops.gemm_f16(s["a"], s["b"], s["c"])
+        if self.dtype_name == "bf8":
+            return self.ops.gemm_f8(s["a"], s["b"], s["c"], a_scales=s["sa"], b_scales=s["sb"])
+        return self.ops.gemm_mxf4(s["a"], s["b"], s["sa"], s["sb"], s["c"])
+
+    def input_bytes(self) -> int:
+        s = self.sets[0]
+        return sum(t.numel() * t.element_size() for k, t in s.items() if k != "c")
+
+    def set_bytes(self) -> int:
+        s = self.sets[0]
+        return sum(t.numel() * t.element_size() for t in s.values())
+
+
+def time_device(w: Workload, steps: int, warmup: int, world: int) -> float:
+    """ms per step: CUDA events on the launching stream, max over ranks."""
+    for i in range(warmup):
+        w.run(i)
+    barrier(world)
+    stream = torch.cuda.current_stream()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for i in range(steps):
+        w.run(warmup + i)
+    end.record(stream)
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / steps
+    barrier(world)
+    w.ops.check_status()
+    return max_over_ranks(ms, world)
+
+
+def time_e2e(w: Workload, steps: int, warmup: int, world: int) -> tuple[float, int, int]:
+    """Public-API call with host inputs: pinned H2D of A and B (and scales),
+    the GEMM, D2H of C - all inside the timed region every step."""
+    s = w.sets[0]
+    host = {k: torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for k, t in s.items()}
+    for k, t in s.items():
+        if k != "c":
+            host[k].copy_(t)
+    dev = {k: torch.empty_like(t) for k, t in s.items()}
+    h2d = sum(host[k].numel() * host[k].element_size() for k in host if k != "c")
+    d2h = host["c"].numel() * host["c"].element_size()
+    ops = w.ops
+
+    def step():
+        for k in host:
+            if k != "c":
+                dev[k].copy_(host[k], non_blocking=True)
+        if w.dtype_name in ("fp16", "bf16"):
+            from gfx950_gluon_tutorials_b200 import a16w16
+            c = a16w16.matmul(dev["a"], dev["b"].T)
+        elif w.dtype_name == "bf8":
+            from gfx950_gluon_tutorials_b200 import a8w8
+            c = a8w8.matmul_scaled(dev["a"], dev["b"].T, dev["sa"], dev["sb"])
+        else:
+            from gfx950_gluon_tutorials_b200 import a4w4
+            c = a4w4.matmul(dev["a"], dev["b"], dev["sa"], dev["sb"])
+        host["c"].copy_(c, non_blocking=True)
+
+    for _ in range(warmup):
+        step()
+    barrier(world)
+    stream = torch.cuda.current_stream()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        step()
+    end.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(start.elapsed_time(end) / steps, world)
+    ops.check_status()
+    return ms, h2d, d2h
+
+
+def time_allgather(w: Workload, world: int, iters: int = 10) -> dict | None:
+    """Separately timed NCCL all-gather of every rank's C slab into a
+    [world][M][N/world] buffer in each GPU's own memory."""
+    if world == 1:
+        return None
+    c = w.sets[0]["c"]
+    out = torch.empty((world,) + tuple(c.shape), dtype=c.dtype, device=c.device)
+    for _ in range(3):
+        torch.distributed.all_gather_into_tensor(out, c)
+    barrier(world)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(iters):
+        torch.distributed.all_gather_into_tensor(out, c)
+    end.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(start.elapsed_time(end) / iters, world)
+    total = out.numel() * out.element_size()
+    return {"bytes": total, "ms": ms, "algbw_gbs": total / ms / 1e6,
+            "busbw_gbs": total * (world - 1) / world / ms / 1e6}
+
+
+def cpu_reference_tflops(M: int, N: int, K: int, budget_s: float, threads: int) -> dict:
+    """The reference's CPU path (oracle restatement: torch.matmul in fp16 on the
+    host cores, kernels/gemm/intra_wave/a16w16/bench.py:183) on a row sample of
+    the same workload, repeated until about `budget_s` seconds of work."""
+    from oracle import reference_cpu
+    return reference_cpu.time_a16w16(M, N, K, budget_s=budget_s, threads=threads)
+
+
+def read_traffic(kernel_key: str):
+    try:
+        with open(TRAFFIC_PATH) as f:
+            return json.load(f).get(kernel_key)
+    except (OSError, ValueError):
+        return None
+
+
+# ---------------------------------------------------------------- contract --
+def contract_main(args):
+    rank, world, local = dist_setup(args.gpus)
+    if args.impl == "reference":
+        return reference_main(args, rank, world)
+    import gfx950_gluon_tutorials_b200 as pkg
+    pkg.lib()  # the CUDA library must load; there is no fallback
+    peaks, peak_src = load_peaks()
+    M, K = 4096, 8192
+    n_local = 4096
+    if args.config == "large":
+        M, K = 16384, 16384
+        n_local = 53248 // world
+    results = {}
+    clocks = ClockSampler(local)
+    head_name = "mxfp4" if args.config == "large" else args.dtype
+    # enough rotating sets that one pass over them exceeds the 126 MB L2
+    w = Workload("head", M, n_local, K, head_name, sets=1, seed=1234 + rank)
+    per_set = w.set_bytes()
+    nsets = max(2, min(8, int(640e6 // per_set) + 1))
+    if args.config == "large":
+        nsets = 2
+    w = Workload("head", M, n_local, K, head_name, sets=nsets, seed=1234 + rank)
+    clocks.start()
+    ms = time_device(w, args.steps, args.warmup, world)
+    clock_info = clocks.stop()
+    flops_total = w.flops * world
+    value = flops_total / (ms * 1e-3) / 1e12
+    per_gpu = value / world
+    peak = tensor_peak(head_name, peaks)
+    results["head"] = dict(ms=ms, tflops=value)
+    by_dtype = {}
+    if args.config != "large" and not args.no_extra:
+        for dn in ("bf8", "mxfp4"):
+            wx = Workload(dn, M, n_local, K, dn, sets=4, seed=99 + rank)
+            msx = time_device(wx, args.steps, args.warmup, world)
+            tf = wx.flops * world / (msx * 1e-3) / 1e12
+            by_dtype[dn] = {
+                "ms_per_step": msx, "tflops": tf, "tflops_per_gpu": tf / world,
+                "pct_of_nominal_dense_peak": 100.0 * tf / world / NOMINAL_DENSE_TFLOPS[dn],
+                "frac_of_measured": tf / world / tensor_peak(dn, peaks),
+                "launches_per_step": wx.launches_per_step}
+            del wx
+            torch.cuda.empty_cache()
+    e2e_ms, h2d, d2h = time_e2e(w, max(3, args.steps // 5), min(args.warmup, 3), world)
+    e2e_val = flops_total / (e2e_ms * 1e-3) / 1e12
+    gather = time_allgather(w, world)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_reference_tflops(M, n_local, K, args.cpu_budget, os.cpu_count() or 1)
+    if world > 1:
+        barrier(world)
+    if rank == 0:
+        traffic = read_traffic(f"{head_name}_{M}x{n_local}x{K}")
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "TFLOPS",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms,
+            "higher_is_better": True,
+            "scaling": "strong" if args.config == "large" else "weak",
+            "vs_baseline": None,
+            "dtype": head_name,
+            "data": "synthetic (seeded N(0,1) inputs, BASELINE recipes)",
+            "config": {
+                "workload": ("a4w4 MXFP4 16384x53248x16384, B split along N over the ranks "
+                             "(BASELINE configs[4])" if args.config == "large" else
+                             f"a16w16 {head_name} C=A*B^T M=4096 K=8192, 4096 columns of C per "
+                             "GPU, B sharded along N, A replicated (BASELINE configs[1])"),
+                "M": M, "N_per_gpu": n_local, "K": K, "N_total": n_local * world,
+                "parallelism": f"N-shard x{world}, no collective in the timed loop",
+                "l2": f"rotating {nsets} input sets, {nsets * per_set / 1e6:.0f} MB > 126 MB L2",
+            },
+            "tflops_per_gpu": per_gpu,
+            "pct_of_nominal_dense_peak": 100.0 * per_gpu / NOMINAL_DENSE_TFLOPS[head_name],
+            "by_dtype": by_dtype,
+            "roofline": {
+                "bound": "tensor", "achieved": per_gpu, "peak": peak, "unit": "TFLOP/s",
+                "frac": per_gpu / peak, "traffic": traffic,
+                "peak_source": (f"{peak_src} bf16_tflops (burst) x dtype ratio"
+                                if head_name != "fp16" else f"{peak_src} bf16_tflops (burst)"),
+                "algorithmic_flops_per_launch": w.flops,
+                "algorithmic_bytes_per_launch": w.input_bytes() + w.sets[0]["c"].numel() * 2,
+            },
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_val, "unit": "TFLOPS", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+                    "path": "public API (a16w16.matmul etc.) with pinned host buffers"},
+            "gpu_launches": args.steps * w.launches_per_step,
+            "clocks": clock_info,
+        }
+        if gather is not None:
+            line["allgather"] = gather
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+def reference_main(args, rank, world):
+    """CPU reference arm: rank 0 times the reference path; other ranks exit."""
+    if rank != 0:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return
+    M, K, n_local = 4096, 8192, 4096
+    threads = os.cpu_count() or 1
+    from oracle import reference_cpu
+    vals = []
+    info = None
+    for i in range(args.warmup + args.steps):
+        info = reference_cpu.time_a16w16(M, n_local, K, budget_s=args.ref_step_s,
+                                         threads=threads)
+        if i >= args.warmup:
+            vals.append(info["value"])
+    value = statistics.median(vals)
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
+        "data": "synthetic (seeded N(0,1) inputs)", "impl": "reference",
+        "config": {"workload": "a16w16 fp16 C=A*B^T M=4096 N=4096 K=8192 (BASELINE configs[1]) "
+                               "on the host cores", "M": M, "N_per_gpu": n_local, "K": K},
+        "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": threads, "kind": "port",
+                         "sample": info["sample"]},
+        "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+# ------------------------------------------------- reference bench surface --
+def reference_surface_main(args):
+    """kernels/gemm/intra_wave/<kind>/bench.py: correctness then a TFLOPS table."""
+    from gfx950_gluon_tutorials_b200 import a4w4, a8w8, a16w16, ops
+    torch.cuda.set_device(0)
+    ks = [args.K] if args.K else [512, 1024, 2048, 4096, 8192, 16384, 32768]
+    M, N = args.M, args.N
+    dtypes = args.dtype or (["fp16", "bf16"] if args.kernel == "a16w16" else ["-"])
+    rows = []
+    for dn in dtypes:
+        for K in ks:
+            if args.kernel == "a16w16":
+                dt = torch.float16 if dn == "fp16" else torch.bfloat16
+                a = torch.rand((M, K), device="cuda", dtype=dt) - 0.5
+                b = torch.rand((N, K), device="cuda", dtype=dt).T - 0.5
+                ok = torch.allclose(a16w16.matmul(a, b), torch.matmul(a, b), atol=1e-1, rtol=0)
+                fn = lambda: a16w16.matmul(a, b)  # noqa: E731
+                elem = a.element_size()
+            elif args.kernel == "a8w8":
+                a = (torch.rand((M, K), device="cuda", dtype=torch.float16) - 0.5).to(
+                    torch.float8_e5m2)
+                b = (torch.rand((N, K), device="cuda", dtype=torch.float16).T - 0.5).to(
+                    torch.float8_e5m2)
+                ref = torch.matmul(a.to(torch.float16), b.to(torch.float16))
+                ok = torch.allclose(a8w8.matmul(a, b), ref, atol=1e-1, rtol=0)
+                fn = lambda: a8w8.matmul(a, b)  # noqa: E731
+                elem = 1
+            else:
+                gen = torch.Generator().manual_seed(42)
+                a = ((torch.randint(0, 16, (M, K // 2), generator=gen, dtype=torch.uint8) << 4)
+                     | torch.randint(0, 16, (M, K // 2), generator=gen, dtype=torch.uint8)).cuda()
+                b = ((torch.randint(0, 16, (N, K // 2), generator=gen, dtype=torch.uint8) << 4)
+                     | torch.randint(0, 16, (N, K // 2), generator=gen, dtype=torch.uint8)).cuda()
+                m_pad = (M + 255) // 256 * 256
+                sa = torch.randint(124, 128, (K // 32, m_pad), dtype=torch.uint8).cuda().T[:M]
+                sb = torch.randint(124, 128, (K // 32, N), dtype=torch.uint8).cuda().T
+                from oracle import mx
+                ref = mx.bf16_bits_to_f32(mx.gemm_mxfp4_ref(a.cpu().numpy(), b.cpu().numpy(),
+                                                            sa.cpu().numpy(), sb.cpu().numpy()))
+                got = a4w4.matmul(a, b, sa, sb).float().cpu().numpy()
+                ok = bool(abs(got - ref).max() <= 0.1)
+                fn = lambda: a4w4.matmul(a, b, sa, sb)  # noqa: E731
+                elem = 0.5
+            ops.check_status()
+            print(f"[{args.kernel}] M={M} N={N} K={K} dtype={dn}: "
+                  f"{'match' if ok else 'DIFFER'}", flush=True)
+            if args.rocprof:
+                for _ in range(1000):
+                    fn()
+                torch.cuda.synchronize()
+                print(f"[{args.kernel}] M={M} N={N} K={K}: 1000 iterations done", flush=True)
+                continue
+            for _ in range(5):
+                fn()
+            st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            st.record()
+            for _ in range(50):
+                fn()
+            en.record()
+            torch.cuda.synchronize()
+            ms = st.elapsed_time(en) / 50
+            rows.append((M, N, K, dn, 2 * M * N * K / ms / 1e9, (M + N) * K * elem))
+    if rows:
+        print(f"{'M':>6} {'N':>6} {'K':>6} {'dtype':>6} {'TFLOPS':>9}")
+        for M_, N_, K_, dn, tf, _ in rows:
+            print(f"{M_:>6} {N_:>6} {K_:>6} {dn:>6} {tf:>9.1f}")
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__,
+                                 formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b2g", "reference"], default="b2g")
+    ap.add_argument("--config", choices=["default", "large"], default="default")
+    ap.add_argument("--dtype", nargs="+", default=None)
+    ap.add_argument("--no-extra", action="store_true", help="skip the BF8/MXFP4 entries")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    ap.add_argument("--cpu-budget", type=float, default=8.0, help="seconds of CPU baseline work")
+    ap.add_argument("--ref-step-s", type=float, default=4.0,
+                    help="seconds of CPU work per --impl reference step")
+    # reference bench surface
+    ap.add_argument("--kernel", choices=["a16w16", "a8w8", "a4w4"], default=None)
+    ap.add_argument("--version", type=int, default=None, help="accepted for compatibility")
+    ap.add_argument("--K", type=int, default=None)
+    ap.add_argument("--M", type=int, default=4096)
+    ap.add_argument("--N", type=int, default=4096)
+    ap.add_argument("--rocprof", "--profile", dest="rocprof", action="store_true")
+    ap.add_argument("--rotating-buffer-size", type=int, default=512)
+    args = ap.parse_args()
+    if args.kernel is not None:
+        return reference_surface_main(args)
+    if args.dtype is None:
+        args.dtype = "fp16"
+    elif isinstance(args.dtype, list):
+        args.dtype = args.dtype[0]
+    if args.warmup < 3:
+        log("note: raising --warmup to 3 (timing rule)")
+        args.warmup = 3
+    contract_main(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,547 @@
+// extern "C" entry points of libb2g.so: argument checks, TMA descriptors,
+// workspace carving, scheduler planning and kernel launches.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "b2g.h"
+#include "gemm_kernel.cuh"
+#include "pack.cuh"
+#include "sched.h"
+
+using namespace b2g;
+
+namespace {
+
+// ------------------------------------------------------------- options --
+struct Options {
+  std::atomic<int64_t> pair_f16{1};      // cta_group::2 for f16/bf16/e5m2
+  std::atomic<int64_t> sk_mode{1};       // see make_plan
+  std::atomic<int64_t> group_m{8};
+  std::atomic<int64_t> min_sk_iters{4};
+  std::atomic<int64_t> timeout_ms{2000};
+  std::atomic<int64_t> inject{0};
+  std::atomic<int64_t> max_units{0};     // 0 = one unit per SM (pair)
+};
+Options g_opt;
+
+constexpr int kMaxDevices = 64;
+
+int device_sms(int dev) {
+  static std::atomic<int> cache[kMaxDevices];
+  if (dev < 0 || dev >= kMaxDevices) return -1;
+  int v = cache[dev].load();
+  if (v > 0) return v;
+  int sms = 0, major = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -1;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+    return -1;
+  if (major != 10) return -1;
+  cache[dev].store(sms);
+  return sms;
+}
+
+int current_sms() {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+  return device_sms(dev);
+}
+
+// Stream-K owners wait for higher-numbered units, so every unit of a launch
+// must be resident at once: cap the CTA-pair count at what the device can
+// co-schedule (GPCs may not split evenly into pairs).
+int pair_capacity(int dev, int sms) {
+  static std::atomic<int> cache[kMaxDevices];
+  if (dev < 0 || dev >= kMaxDevices) return sms / 2;
+  int v = cache[dev].load();
+  if (v > 0) return v;
+  constexpr int kStages = 6;
+  using SP = SmemPlan<kKindF16, 2, kStages>;
+  auto kern = gemm_kernel<kKindF16, 2, kStages, false>;
+  int n = 0;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(SP::kDynBytes)) == cudaSuccess) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(sms & ~1), 1, 1);
+    cfg.blockDim = dim3(192, 1, 1);
+    cfg.dynamicSmemBytes = SP::kDynBytes;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = 0;
+  }
+  cudaGetLastError();  // a failed query must not leak into the caller's error state
+  v = (n > 0 && n < sms / 2) ? n : sms / 2;
+  if (n <= 0) v = sms / 2 - 2;  // unknown: leave headroom
+  cache[dev].store(v);
+  return v;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+bool is_scaled(int kind) { return kind == B2G_KIND_MXE5M2 || kind == B2G_KIND_MXFP4; }
+
+int64_t row_bytes(int kind, int64_t K) {
+  switch (kind) {
+    case B2G_KIND_F16:
+    case B2G_KIND_BF16: return 2 * K;
+    case B2G_KIND_E5M2:
+    case B2G_KIND_MXE5M2: return K;
+    default: return K / 2;
+  }
+}
+
+size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
+
+struct Geometry {
+  int cg;
+  SkPlan plan;
+  int launched;
+  int sf_groups;
+  int sfa_row_blocks, sfb_row_blocks;
+  size_t flags_off, flags_bytes, partial_off, partial_bytes;
+  size_t sfa_off, sfa_bytes, sfb_off, sfb_bytes, total;
+};
+
+// `pair_cap`: how many CTA pairs the device can hold at once (0 = sms / 2).
+Geometry geometry(int kind, int M, int N, int K, int sms, int pair_cap = 0) {
+  Geometry g{};
+  g.cg = (!is_scaled(kind) && g_opt.pair_f16.load() != 0) ? 2 : 1;
+  int units = g.cg == 2 ? sms / 2 : sms;
+  if (g.cg == 2 && pair_cap > 0 && pair_cap < units) units = pair_cap;
+  const int64_t mu = g_opt.max_units.load();
+  if (mu > 0 && mu < units) units = static_cast<int>(mu);
+  if (units < 1) units = 1;
+  const int tiles_m = (M + 128 * g.cg - 1) / (128 * g.cg);
+  const int tiles_n = (N + 255) / 256;
+  const int k_iters = static_cast<int>((row_bytes(kind, K) + 127) / 128);
+  g.plan = make_plan(tiles_m, tiles_n, k_iters, units, static_cast<int>(g_opt.group_m.load()),
+                     static_cast<int>(g_opt.sk_mode.load()),
+                     static_cast<int>(g_opt.min_sk_iters.load()));
+  g.launched = std::min(units, std::max(g.plan.dp_tiles, g.plan.sk_units));
+  if (g.launched < 1) g.launched = 1;
+  const int gps = kind == B2G_KIND_MXFP4 ? 2 : 1;
+  g.sf_groups = is_scaled(kind) ? k_iters * gps : 0;
+  g.sfa_row_blocks = is_scaled(kind) ? tiles_m * g.cg : 0;
+  g.sfb_row_blocks = is_scaled(kind) ? tiles_n * 2 : 0;
+  size_t off = 0;
+  g.flags_off = off;
+  g.flags_bytes = align256(static_cast<size_t>(g.plan.sk_units) * g.cg * 4 * sizeof(uint32_t));
+  off += g.flags_bytes;
+  g.partial_off = off;
+  g.partial_bytes = static_cast<size_t>(g.plan.sk_units) * g.cg * 128 * 256 * sizeof(float);
+  off += align256(g.partial_bytes);
+  g.sfa_off = off;
+  g.sfa_bytes = static_cast<size_t>(g.sfa_row_blocks) * g.sf_groups * 512;
+  off += align256(g.sfa_bytes);
+  g.sfb_off = off;
+  g.sfb_bytes = static_cast<size_t>(g.sfb_row_blocks) * g.sf_groups * 512;
+  off += align256(g.sfb_bytes);
+  g.total = off;
+  return g;
+}
+
+int encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner,
+              uint64_t outer, uint64_t stride_bytes, uint32_t box_in, uint32_t box_out,
+              CUtensorMapSwizzle sw) {
+  auto enc = tensor_map_encoder();
+  if (enc == nullptr) return B2G_ETENSORMAP;
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {stride_bytes};
+  const cuuint32_t box[2] = {box_in, box_out};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? B2G_OK : B2G_ETENSORMAP;
+}
+
+template <int KIND, int CG, bool OB>
+int launch_gemm_t(const GemmParams& prm, int units, cudaStream_t stream) {
+  constexpr int kStages = CG == 1 ? 4 : 6;
+  using SP = SmemPlan<KIND, CG, kStages>;
+  static_assert(SP::kDynBytes <= 232448, "shared memory plan exceeds 227 KB");
+  auto kern = gemm_kernel<KIND, CG, kStages, OB>;
+  static std::atomic<uint64_t> attr_done{0};  // bit per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = 1ull << (dev & 63);
+  if ((attr_done.load() & bit) == 0) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(SP::kDynBytes));
+    if (e != cudaSuccess) return static_cast<int>(e);
+    attr_done.fetch_or(bit);
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(units * CG), 1, 1);
+  cfg.blockDim = dim3(192, 1, 1);
+  cfg.dynamicSmemBytes = SP::kDynBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  if (CG == 2) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, prm);
+  return e == cudaSuccess ? B2G_OK : static_cast<int>(e);
+}
+
+template <int KIND, int CG>
+int launch_gemm_out(const GemmParams& prm, int units, int out_dtype, cudaStream_t s) {
+  return out_dtype == B2G_DT_BF16 ? launch_gemm_t<KIND, CG, true>(prm, units, s)
+                                  : launch_gemm_t<KIND, CG, false>(prm, units, s);
+}
+
+int dispatch(int kind, int cg, const GemmParams& prm, int units, int out_dtype,
+             cudaStream_t s) {
+  switch (kind) {
+    case B2G_KIND_F16:
+      return cg == 2 ? launch_gemm_out<kKindF16, 2>(prm, units, out_dtype, s)
+                     : launch_gemm_out<kKindF16, 1>(prm, units, out_dtype, s);
+    case B2G_KIND_BF16:
+      return cg == 2 ? launch_gemm_out<kKindBF16, 2>(prm, units, out_dtype, s)
+                     : launch_gemm_out<kKindBF16, 1>(prm, units, out_dtype, s);
+    case B2G_KIND_E5M2:
+      return cg == 2 ? launch_gemm_out<kKindE5M2, 2>(prm, units, out_dtype, s)
+                     : launch_gemm_out<kKindE5M2, 1>(prm, units, out_dtype, s);
+    case B2G_KIND_MXE5M2: return launch_gemm_out<kKindMXE5M2, 1>(prm, units, out_dtype, s);
+    case B2G_KIND_MXFP4: return launch_gemm_out<kKindMXFP4, 1>(prm, units, out_dtype, s);
+    default: return B2G_EINVAL;
+  }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+struct GemmCall {
+  int kind;
+  const void* A;
+  int64_t lda;  // elements of A's storage type
+  const void* B;
+  int64_t ldb;
+  const uint8_t* sfa;
+  int64_t sfa_s0, sfa_s1;
+  const uint8_t* sfb;
+  int64_t sfb_s0, sfb_s1;
+  void* C;
+  int64_t ldc;
+  int M, N, K, out_dtype;
+  void* ws;
+  size_t ws_bytes;
+  int* status;
+  cudaStream_t stream;
+};
+
+// Storage bytes per stored element of A/B (packed e2m1: one byte holds 2).
+int64_t storage_elem_bytes(int kind) {
+  return (kind == B2G_KIND_F16 || kind == B2G_KIND_BF16) ? 2 : 1;
+}
+
+int check_call(const GemmCall& c) {
+  if (c.kind < B2G_KIND_F16 || c.kind > B2G_KIND_MXFP4) return B2G_EINVAL;
+  if (c.out_dtype != B2G_DT_F16 && c.out_dtype != B2G_DT_BF16) return B2G_EINVAL;
+  if (c.A == nullptr || c.B == nullptr || c.C == nullptr) return B2G_EINVAL;
+  if (c.M < 1 || c.N < 1 || c.K < 1) return B2G_ESHAPE;
+  if (is_scaled(c.kind) && (c.K % 32) != 0) return B2G_ESHAPE;
+  if (c.kind == B2G_KIND_MXFP4 && (c.K % 2) != 0) return B2G_ESHAPE;
+  if (c.M > (1 << 30) || c.N > (1 << 30) || c.K > (1 << 30)) return B2G_ESHAPE;
+  if (is_scaled(c.kind) && (c.sfa == nullptr || c.sfb == nullptr)) return B2G_EINVAL;
+  const int64_t eb = storage_elem_bytes(c.kind);
+  const int64_t rb = row_bytes(c.kind, c.K);
+  if (!aligned16(c.A) || !aligned16(c.B) || !aligned16(c.C)) return B2G_EALIGN;
+  if ((c.lda * eb) % 16 != 0 || (c.ldb * eb) % 16 != 0 || (c.ldc * 2) % 16 != 0)
+    return B2G_EALIGN;
+  if (c.lda * eb < rb || c.ldb * eb < rb || c.ldc < c.N) return B2G_ESTRIDE;
+  if (is_scaled(c.kind) && (c.sfa_s0 < 0 || c.sfa_s1 < 0 || c.sfb_s0 < 0 || c.sfb_s1 < 0))
+    return B2G_ESTRIDE;
+  return B2G_OK;
+}
+
+int run_gemm(const GemmCall& c) {
+  int rc = check_call(c);
+  if (rc != B2G_OK) return rc;
+  int dev = -1;
+  cudaGetDevice(&dev);
+  const int sms = current_sms();
+  if (sms <= 0) return B2G_ENODEVICE;
+  const Geometry g = geometry(c.kind, c.M, c.N, c.K, sms, pair_capacity(dev, sms));
+  if (g.total > 0 && (c.ws == nullptr || c.ws_bytes < g.total)) return B2G_EWORKSPACE;
+  if (c.ws != nullptr && (reinterpret_cast<uintptr_t>(c.ws) & 255u) != 0) return B2G_EALIGN;
+  uint8_t* ws = static_cast<uint8_t*>(c.ws);
+
+  GemmParams prm;
+  std::memset(&prm, 0, sizeof(prm));
+  const int64_t eb = storage_elem_bytes(c.kind);
+  const uint64_t rb = static_cast<uint64_t>(row_bytes(c.kind, c.K));
+  rc = encode_2d(&prm.tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, c.A, rb, static_cast<uint64_t>(c.M),
+                 static_cast<uint64_t>(c.lda * eb), 128, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc != B2G_OK) return rc;
+  rc = encode_2d(&prm.tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, c.B, rb, static_cast<uint64_t>(c.N),
+                 static_cast<uint64_t>(c.ldb * eb), 128, g.cg == 1 ? 256 : 128,
+                 CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc != B2G_OK) return rc;
+  rc = encode_2d(&prm.tmC, CU_TENSOR_MAP_DATA_TYPE_UINT16, c.C, static_cast<uint64_t>(c.N),
+                 static_cast<uint64_t>(c.M), static_cast<uint64_t>(c.ldc * 2), 32, 32,
+                 CU_TENSOR_MAP_SWIZZLE_64B);
+  if (rc != B2G_OK) return rc;
+
+  if (is_scaled(c.kind)) {
+    uint8_t* sfa_blk = ws + g.sfa_off;
+    uint8_t* sfb_blk = ws + g.sfb_off;
+    cudaError_t e = launch_sf_relayout(c.sfa, c.sfa_s0, c.sfa_s1, c.M, c.K / 32,
+                                       g.sfa_row_blocks, g.sf_groups, sfa_blk, c.stream);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    e = launch_sf_relayout(c.sfb, c.sfb_s0, c.sfb_s1, c.N, c.K / 32, g.sfb_row_blocks,
+                           g.sf_groups, sfb_blk, c.stream);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    prm.sfa = sfa_blk;
+    prm.sfb = sfb_blk;
+  }
+  prm.partials = g.partial_bytes ? reinterpret_cast<float*>(ws + g.partial_off) : nullptr;
+  prm.flags = g.flags_bytes ? reinterpret_cast<uint32_t*>(ws + g.flags_off) : nullptr;
+  prm.status = c.status;
+  prm.plan = g.plan;
+  prm.M = c.M;
+  prm.N = c.N;
+  prm.K = c.K;
+  prm.sf_groups = g.sf_groups;
+  prm.inject = static_cast<int32_t>(g_opt.inject.load());
+  prm.timeout_ns = static_cast<uint64_t>(g_opt.timeout_ms.load()) * 1000000ull;
+  return dispatch(c.kind, g.cg, prm, g.launched, c.out_dtype, c.stream);
+}
+
+}  // namespace
+
+extern "C" {
+
+int b2g_version(void) { return 100; }
+
+const char* b2g_strerror(int code) {
+  if (code >= B2G_STATUS_TIMEOUT && code < B2G_STATUS_TIMEOUT + 0x100) {
+    switch (code & 0xFF) {
+      case B2G_SITE_EMPTY: return "timeout: producer waiting for a free ring slot";
+      case B2G_SITE_FULL: return "timeout: MMA waiting for a filled ring slot";
+      case B2G_SITE_ACC_EMPTY: return "timeout: MMA waiting for a drained accumulator";
+      case B2G_SITE_ACC_FULL: return "timeout: epilogue waiting for an accumulator";
+      case B2G_SITE_OVERLAP: return "timeout: MMA waiting for shared accumulator columns";
+      case B2G_SITE_FLAG: return "timeout: stream-K owner waiting for a contributor";
+      default: return "timeout in a bounded wait";
+    }
+  }
+  switch (code) {
+    case B2G_OK: return "ok";
+    case B2G_EINVAL: return "invalid argument (kind, dtype or null pointer)";
+    case B2G_ESHAPE: return "unsupported shape (M, N, K range or K multiple)";
+    case B2G_EALIGN: return "pointer or row stride not 16-byte aligned";
+    case B2G_ESTRIDE: return "operand not K-contiguous or row stride too small";
+    case B2G_EWORKSPACE: return "workspace missing or too small";
+    case B2G_ETENSORMAP: return "TMA descriptor rejected by the driver";
+    case B2G_ENODEVICE: return "no sm_100 device is current";
+    case B2G_ECAPACITY: return "size exceeds the entry point's fixed capacity";
+    default: break;
+  }
+  if (code > 0) return cudaGetErrorString(static_cast<cudaError_t>(code));
+  return "unknown error";
+}
+
+size_t b2g_gemm_workspace_bytes(int kind, int M, int N, int K) {
+  if (kind < B2G_KIND_F16 || kind > B2G_KIND_MXFP4 || M < 1 || N < 1 || K < 1) return 0;
+  int dev = -1;
+  cudaGetDevice(&dev);
+  const int sms = current_sms();
+  if (sms <= 0) return 0;
+  return geometry(kind, M, N, K, sms, pair_capacity(dev, sms)).total;
+}
+
+int b2g_workspace_reset(void* workspace, size_t bytes, void* stream) {
+  if (workspace == nullptr || bytes == 0) return B2G_OK;
+  const cudaError_t e = cudaMemsetAsync(workspace, 0, bytes, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? B2G_OK : static_cast<int>(e);
+}
+
+int b2g_gemm_f16(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
+                 int M, int N, int K, int in_dtype, int out_dtype, void* workspace,
+                 size_t workspace_bytes, int* status, void* stream) {
+  if (in_dtype != B2G_DT_F16 && in_dtype != B2G_DT_BF16) return B2G_EINVAL;
+  GemmCall c{};
+  c.kind = in_dtype == B2G_DT_F16 ? B2G_KIND_F16 : B2G_KIND_BF16;
+  c.A = A; c.lda = lda; c.B = B; c.ldb = ldb; c.C = C; c.ldc = ldc;
+  c.M = M; c.N = N; c.K = K; c.out_dtype = out_dtype;
+  c.ws = workspace; c.ws_bytes = workspace_bytes; c.status = status;
+  c.stream = static_cast<cudaStream_t>(stream);
+  return run_gemm(c);
+}
+
+int b2g_gemm_f8(const void* A, int64_t lda, const void* B, int64_t ldb, const uint8_t* sfa,
+                int64_t sfa_s0, int64_t sfa_s1, const uint8_t* sfb, int64_t sfb_s0,
+                int64_t sfb_s1, void* C, int64_t ldc, int M, int N, int K, int out_dtype,
+                void* workspace, size_t workspace_bytes, int* status, void* stream) {
+  if ((sfa == nullptr) != (sfb == nullptr)) return B2G_EINVAL;
+  GemmCall c{};
+  c.kind = sfa == nullptr ? B2G_KIND_E5M2 : B2G_KIND_MXE5M2;
+  c.A = A; c.lda = lda; c.B = B; c.ldb = ldb;
+  c.sfa = sfa; c.sfa_s0 = sfa_s0; c.sfa_s1 = sfa_s1;
+  c.sfb = sfb; c.sfb_s0 = sfb_s0; c.sfb_s1 = sfb_s1;
+  c.C = C; c.ldc = ldc; c.M = M; c.N = N; c.K = K; c.out_dtype = out_dtype;
+  c.ws = workspace; c.ws_bytes = workspace_bytes; c.status = status;
+  c.stream = static_cast<cudaStream_t>(stream);
+  return run_gemm(c);
+}
+
+int b2g_gemm_mxf4(const uint8_t* A, int64_t lda, const uint8_t* B, int64_t ldb,
+                  const uint8_t* sfa, int64_t sfa_s0, int64_t sfa_s1, const uint8_t* sfb,
+                  int64_t sfb_s0, int64_t sfb_s1, void* C, int64_t ldc, int M, int N, int K,
+                  int out_dtype, void* workspace, size_t workspace_bytes, int* status,
+                  void* stream) {
+  GemmCall c{};
+  c.kind = B2G_KIND_MXFP4;
+  c.A = A; c.lda = lda; c.B = B; c.ldb = ldb;
+  c.sfa = sfa; c.sfa_s0 = sfa_s0; c.sfa_s1 = sfa_s1;
+  c.sfb = sfb; c.sfb_s0 = sfb_s0; c.sfb_s1 = sfb_s1;
+  c.C = C; c.ldc = ldc; c.M = M; c.N = N; c.K = K; c.out_dtype = out_dtype;
+  c.ws = workspace; c.ws_bytes = workspace_bytes; c.status = status;
+  c.stream = static_cast<cudaStream_t>(stream);
+  return run_gemm(c);
+}
+
+int b2g_quant_mxfp4(const float* src, int64_t ld, int rows, int K, uint8_t* q, int64_t ldq,
+                    uint8_t* scales, int64_t sc_s0, int64_t sc_s1, void* stream) {
+  if (src == nullptr || q == nullptr || scales == nullptr) return B2G_EINVAL;
+  if (rows < 1 || K < 32 || K % 32 != 0) return B2G_ESHAPE;
+  if (!aligned16(src) || (ld % 4) != 0 || (reinterpret_cast<uintptr_t>(q) & 3u) != 0 ||
+      (ldq % 4) != 0)
+    return B2G_EALIGN;
+  if (ld < K || ldq < K / 2 || sc_s0 < 0 || sc_s1 < 0) return B2G_ESTRIDE;
+  const cudaError_t e = launch_quant_mxfp4(src, ld, rows, K, q, ldq, scales, sc_s0, sc_s1,
+                                           static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? B2G_OK : static_cast<int>(e);
+}
+
+int b2g_quant_mxe5m2(const float* src, int64_t ld, int rows, int K, const uint8_t* scales,
+                     int64_t sc_s0, int64_t sc_s1, uint8_t* q, int64_t ldq, void* stream) {
+  if (src == nullptr || q == nullptr || scales == nullptr) return B2G_EINVAL;
+  if (rows < 1 || K < 32 || K % 32 != 0) return B2G_ESHAPE;
+  if (!aligned16(src) || (ld % 4) != 0 || (reinterpret_cast<uintptr_t>(q) & 7u) != 0 ||
+      (ldq % 8) != 0)
+    return B2G_EALIGN;
+  if (ld < K || ldq < K || sc_s0 < 0 || sc_s1 < 0) return B2G_ESTRIDE;
+  const cudaError_t e = launch_quant_mxe5m2(src, ld, rows, K, scales, sc_s0, sc_s1, q, ldq,
+                                            static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? B2G_OK : static_cast<int>(e);
+}
+
+int b2g_cast_e5m2(const void* src, int src_dtype, int64_t n, uint8_t* dst, void* stream) {
+  if (src == nullptr || dst == nullptr) return B2G_EINVAL;
+  if (src_dtype != B2G_DT_F16 && src_dtype != B2G_DT_BF16 && src_dtype != B2G_DT_F32)
+    return B2G_EINVAL;
+  if (n < 0) return B2G_ESHAPE;
+  if (n == 0) return B2G_OK;
+  const cudaError_t e =
+      launch_cast_e5m2(src, src_dtype, n, dst, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? B2G_OK : static_cast<int>(e);
+}
+
+int b2g_set_option(int key, int64_t value) {
+  switch (key) {
+    case B2G_OPT_PAIR: g_opt.pair_f16.store(value != 0); return B2G_OK;
+    case B2G_OPT_SK_MODE:
+      if (value < 0 || value > 2) return B2G_EINVAL;
+      g_opt.sk_mode.store(value);
+      return B2G_OK;
+    case B2G_OPT_GROUP_M:
+      if (value < 1 || value > 64) return B2G_EINVAL;
+      g_opt.group_m.store(value);
+      return B2G_OK;
+    case B2G_OPT_MIN_SK_ITERS:
+      if (value < 1) return B2G_EINVAL;
+      g_opt.min_sk_iters.store(value);
+      return B2G_OK;
+    case B2G_OPT_TIMEOUT_MS:
+      if (value < 1 || value > 60000) return B2G_EINVAL;
+      g_opt.timeout_ms.store(value);
+      return B2G_OK;
+    case B2G_OPT_INJECT_FLAG_TIMEOUT: g_opt.inject.store(value != 0); return B2G_OK;
+    case B2G_OPT_MAX_UNITS:
+      if (value < 0) return B2G_EINVAL;
+      g_opt.max_units.store(value);
+      return B2G_OK;
+    default: return B2G_EINVAL;
+  }
+}
+
+int64_t b2g_get_option(int key) {
+  switch (key) {
+    case B2G_OPT_PAIR: return g_opt.pair_f16.load();
+    case B2G_OPT_SK_MODE: return g_opt.sk_mode.load();
+    case B2G_OPT_GROUP_M: return g_opt.group_m.load();
+    case B2G_OPT_MIN_SK_ITERS: return g_opt.min_sk_iters.load();
+    case B2G_OPT_TIMEOUT_MS: return g_opt.timeout_ms.load();
+    case B2G_OPT_INJECT_FLAG_TIMEOUT: return g_opt.inject.load();
+    case B2G_OPT_MAX_UNITS: return g_opt.max_units.load();
+    default: return -1;
+  }
+}
+
+int b2g_plan_query(int kind, int M, int N, int K, int num_sms, int32_t* out, int out_len) {
+  if (out == nullptr || out_len < 9) return B2G_EINVAL;
+  if (kind < B2G_KIND_F16 || kind > B2G_KIND_MXFP4 || M < 1 || N < 1 || K < 1 || num_sms < 2)
+    return B2G_EINVAL;
+  const Geometry g = geometry(kind, M, N, K, num_sms);
+  out[0] = g.cg;
+  out[1] = g.plan.tiles_m;
+  out[2] = g.plan.tiles_n;
+  out[3] = g.plan.k_iters;
+  out[4] = g.plan.units;
+  out[5] = g.plan.dp_tiles;
+  out[6] = g.plan.sk_units;
+  out[7] = g.launched;
+  out[8] = g.plan.group_m;
+  return B2G_OK;
+}
+
+int b2g_plan_items(int kind, int M, int N, int K, int num_sms, int unit, int32_t* items,
+                   int max_items) {
+  if (kind < B2G_KIND_F16 || kind > B2G_KIND_MXFP4 || M < 1 || N < 1 || K < 1 || num_sms < 2)
+    return B2G_EINVAL;
+  const Geometry g = geometry(kind, M, N, K, num_sms);
+  if (unit < 0 || unit >= g.launched) return 0;
+  WorkCursor cur = cursor_begin(g.plan, unit);
+  WorkItem w;
+  int n = 0;
+  while (cursor_next(g.plan, unit, cur, w)) {
+    if (items != nullptr && n < max_items) {
+      int32_t* o = items + 8 * n;
+      o[0] = w.tile; o[1] = w.tm; o[2] = w.tn; o[3] = w.k_begin;
+      o[4] = w.k_end; o[5] = w.role; o[6] = w.first_contrib; o[7] = w.last_contrib;
+    }
+    ++n;
+  }
+  return n;
+}
+
+}  // extern "C"

@@ -1,0 +1,511 @@
+// Persistent, warp-specialised C = A * B^T for sm_100a.
+//
+// Replaces the reference's per-tile Gluon kernels
+//   a16w16  kernels/gemm/intra_wave/a16w16/v9_beyond_hotloop/matmul_kernel.py:32-388
+//   a8w8    kernels/gemm/intra_wave/a8w8/matmul_kernel.py:33-435
+//   a4w4    kernels/gemm/intra_wave/a4w4/v1_sliceMN/matmul_kernel.py:15-694
+// with one template: A is M x K and B is N x K, both K-contiguous; C is M x N.
+//
+// CTA layout (192 threads):
+//   warp 0      TMA producer: one thread fills a STAGES-deep shared-memory ring
+//               (A tile, B tile and, for block-scaled kinds, the E8M0 scales).
+//   warp 1      MMA issuer: allocates all 512 TMEM columns, one thread issues
+//               tcgen05.mma into a double-buffered TMEM accumulator and copies
+//               scale factors smem -> TMEM with tcgen05.cp.
+//   warps 2-5   epilogue: TMEM -> registers -> (stream-K fixup) -> bf16/fp16
+//               -> swizzled smem -> TMA store. Warp w reads TMEM lanes
+//               32*(w%4) .. 32*(w%4)+31.
+//
+// Tiles: cta_group::1 -> 128 x 256 per CTA; cta_group::2 -> 256 x 256 per CTA
+// pair, each CTA loading its own 128 rows of A and its own 128 rows of B (the
+// pair's MMA reads both halves; there is no multicast load anywhere).
+//
+// Every K stage moves 128 bytes of K per row: 64 fp16/bf16, 128 e5m2 or 256
+// packed e2m1 elements, i.e. four MMAs of 32 bytes of K each.
+//
+// All waits are bounded (iteration probes plus a %globaltimer deadline). On a
+// timeout the CTA records a status code, raises a CTA-wide abort flag, drains
+// its in-flight copies and MMAs, frees TMEM and exits.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "b2g.h"
+#include "ptx.cuh"
+#include "sched.h"
+
+namespace b2g {
+
+enum : int {
+  kKindF16 = 0,
+  kKindBF16 = 1,
+  kKindE5M2 = 2,    // unscaled e5m2 x e5m2 (kind::f8f6f4)
+  kKindMXE5M2 = 3,  // e5m2 with E8M0 per 32 K (kind::mxf8f6f4.block_scale)
+  kKindMXFP4 = 4,   // packed e2m1 with E8M0 per 32 K (kind::mxf4.block_scale)
+};
+
+struct alignas(64) GemmParams {
+  CUtensorMap tmA;
+  CUtensorMap tmB;
+  CUtensorMap tmC;
+  const uint8_t* sfa;   // scales of A in the 512-byte blocked layout (scaled kinds)
+  const uint8_t* sfb;   // scales of B, same layout
+  float* partials;      // stream-K partial tiles, one 128 x 256 fp32 slot per CTA
+  uint32_t* flags;      // stream-K flags, one per (unit, CTA of pair, epilogue warp)
+  int* status;          // device status word, may be null
+  SkPlan plan;
+  int32_t M, N, K;
+  int32_t sf_groups;    // 4-scale groups per 128-row block in the blocked layout
+  int32_t inject;       // test hook: 1 = stream-K owners wait for a flag nobody raises
+  uint64_t timeout_ns;
+};
+
+template <int KIND>
+struct KindTraits {
+  static constexpr bool kScaled = KIND == kKindMXE5M2 || KIND == kKindMXFP4;
+  // 4-scale groups (128 K elements of scales at 32 per scale) per stage.
+  static constexpr int kGroupsPerStage = KIND == kKindMXFP4 ? 2 : 1;
+  // a/b format field of the instruction descriptor.
+  static constexpr uint32_t kFmt = KIND == kKindF16 ? 0u : 1u;
+};
+
+template <int KIND, int CG>
+__device__ __forceinline__ uint32_t make_idesc(uint32_t sf_id) {
+  constexpr uint32_t kM = 128u * CG, kN = 256u;
+  constexpr uint32_t f = KindTraits<KIND>::kFmt;
+  if constexpr (!KindTraits<KIND>::kScaled) {
+    // D fp32 | A fmt | B fmt | K-major both | N >> 3 | M >> 4
+    return (1u << 4) | (f << 7) | (f << 10) | ((kN >> 3) << 17) | ((kM >> 4) << 24);
+  } else {
+    // B scale id | A fmt | B fmt | N >> 3 | scales are E8M0 | M >> 4 | A scale id
+    return (sf_id << 4) | (f << 7) | (f << 10) | ((kN >> 3) << 17) | (1u << 23) |
+           ((kM >> 4) << 24) | (sf_id << 29);
+  }
+}
+
+template <int KIND, int CG, int STAGES>
+struct SmemPlan {
+  static constexpr bool kScaled = KindTraits<KIND>::kScaled;
+  static constexpr int kGps = KindTraits<KIND>::kGroupsPerStage;
+  static constexpr uint32_t kABytes = 128 * 128;
+  static constexpr uint32_t kBRows = CG == 1 ? 256 : 128;
+  static constexpr uint32_t kBBytes = kBRows * 128;
+  static constexpr uint32_t kSfaBytes = kScaled ? kGps * 512 : 0;
+  static constexpr uint32_t kSfbBytes = kScaled ? 2 * kGps * 512 : 0;
+  static constexpr uint32_t kEpiBufs = 2;
+  static constexpr uint32_t kEpiBufBytes = 32 * 64;  // 32 rows x 32 cols x 2 B
+
+  static constexpr uint32_t kAOff = 0;
+  static constexpr uint32_t kBOff = kAOff + STAGES * kABytes;
+  static constexpr uint32_t kSfaOff = kBOff + STAGES * kBBytes;
+  static constexpr uint32_t kSfbOff = kSfaOff + STAGES * kSfaBytes;
+  static constexpr uint32_t kEpiOff = ((kSfbOff + STAGES * kSfbBytes) + 1023u) & ~1023u;
+  static constexpr uint32_t kBarOff = kEpiOff + 4 * kEpiBufs * kEpiBufBytes;
+  // full[S], empty[S], acc_full[2], acc_empty[2], ovl, drain
+  static constexpr uint32_t kNumBars = 2 * STAGES + 6;
+  static constexpr uint32_t kMiscOff = kBarOff + kNumBars * 8;  // tmem slot, abort flag
+  static constexpr uint32_t kBytes = kMiscOff + 16;
+  static constexpr uint32_t kDynBytes = kBytes + 1024;  // + alignment slack
+
+  // bytes landing per stage on the leader's full barrier (both CTAs of a pair)
+  static constexpr uint32_t kTxBytes = CG * (kABytes + kBBytes + kSfaBytes + kSfbBytes);
+
+  // TMEM columns
+  static constexpr uint32_t kAccStride = kScaled ? 224 : 256;
+  static constexpr uint32_t kSfaCol = 480;
+  static constexpr uint32_t kSfbCol = 488;
+};
+
+__device__ __forceinline__ void report_status(const GemmParams& p, int code) {
+  if (p.status != nullptr) atomicCAS(p.status, 0, code);
+}
+
+// Bounded wait on an mbarrier phase. Returns false on timeout or when another
+// warp of the CTA has aborted.
+template <bool kClusterScope>
+__device__ __noinline__ bool wait_phase(uint32_t bar, uint32_t parity, volatile uint32_t* abort_flag,
+                                        const GemmParams& p, int site) {
+  auto probe = [&]() {
+    return kClusterScope ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity);
+  };
+  if (probe()) return true;
+  const uint64_t t0 = globaltimer_ns();
+#pragma unroll 1
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 16; ++i)
+      if (probe()) return true;
+    if (*abort_flag != 0u) return false;
+    if (globaltimer_ns() - t0 > p.timeout_ns) {
+      report_status(p, B2G_STATUS_TIMEOUT | site);
+      *abort_flag = 1u;
+      return false;
+    }
+  }
+}
+
+// Bounded wait for a global stream-K flag to reach `want`.
+__device__ __noinline__ bool wait_flag(const uint32_t* flag, uint32_t want,
+                                       volatile uint32_t* abort_flag, const GemmParams& p,
+                                       int site) {
+  if (ld_acquire_gpu(flag) == want) return true;
+  const uint64_t t0 = globaltimer_ns();
+#pragma unroll 1
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i) {
+      if (ld_acquire_gpu(flag) == want) return true;
+      __nanosleep(64);
+    }
+    if (*abort_flag != 0u) return false;
+    if (globaltimer_ns() - t0 > p.timeout_ns) {
+      report_status(p, B2G_STATUS_TIMEOUT | site);
+      *abort_flag = 1u;
+      return false;
+    }
+  }
+}
+
+template <bool kBF16>
+__device__ __forceinline__ uint32_t pack_out(uint32_t lo, uint32_t hi) {
+  const float a = __uint_as_float(lo), b = __uint_as_float(hi);
+  if constexpr (kBF16) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
+  } else {
+    __half2 v = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+}
+
+__device__ __forceinline__ size_t partial_slot(int32_t unit, uint32_t rank, int CG) {
+  return (static_cast<size_t>(unit) * CG + rank) * (128u * 256u);
+}
+
+__device__ __forceinline__ size_t flag_index(int32_t unit, uint32_t rank, uint32_t quad, int CG) {
+  return (static_cast<size_t>(unit) * CG + rank) * 4u + quad;
+}
+
+template <int KIND, int CG, int STAGES, bool OUT_BF16>
+__global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ GemmParams p) {
+  using SP = SmemPlan<KIND, CG, STAGES>;
+  constexpr bool kScaled = SP::kScaled;
+  constexpr int kGps = SP::kGps;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t warp = threadIdx.x >> 5;
+  const uint32_t lane = threadIdx.x & 31;
+  const uint32_t rank = CG == 2 ? cluster_ctarank() : 0u;
+  const int32_t unit = CG == 2 ? static_cast<int32_t>(blockIdx.x >> 1)
+                               : static_cast<int32_t>(blockIdx.x);
+
+  const uint32_t bar0 = sbase + SP::kBarOff;
+  auto full_bar = [&](uint32_t s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](uint32_t s) { return bar0 + 8u * (STAGES + s); };
+  auto accf_bar = [&](uint32_t b) { return bar0 + 8u * (2 * STAGES + b); };
+  auto acce_bar = [&](uint32_t b) { return bar0 + 8u * (2 * STAGES + 2 + b); };
+  const uint32_t ovl_bar = bar0 + 8u * (2 * STAGES + 4);
+  const uint32_t drain_bar = bar0 + 8u * (2 * STAGES + 5);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SP::kMiscOff);
+  volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + SP::kMiscOff + 4);
+
+  if (threadIdx.x == 0) {
+    for (uint32_t s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (uint32_t b = 0; b < 2; ++b) {
+      mbar_init(accf_bar(b), 1);
+      mbar_init(acce_bar(b), 4 * CG);
+    }
+    mbar_init(ovl_bar, 4 * CG);
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0u;
+    fence_mbarrier_init();
+    prefetch_tensormap(&p.tmA);
+    prefetch_tensormap(&p.tmB);
+    prefetch_tensormap(&p.tmC);
+  }
+  if (warp == 1) {
+    tmem_alloc<CG>(smem_u32(tmem_slot), 512);
+    tmem_relinquish<CG>();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if constexpr (CG == 2) cluster_arrive_wait();
+  tc_fence_after();
+  const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+  const bool leader = (CG == 1) || rank == 0;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer --
+    if (lane == 0) {
+      uint32_t it = 0;
+      WorkCursor cur = cursor_begin(p.plan, unit);
+      WorkItem w;
+      bool alive = true;
+      while (alive && cursor_next(p.plan, unit, cur, w)) {
+        const int32_t a_row = w.tm * (128 * CG) + static_cast<int32_t>(rank) * 128;
+        const int32_t b_row = w.tn * 256 + (CG == 2 ? static_cast<int32_t>(rank) * 128 : 0);
+        for (int32_t k = w.k_begin; k < w.k_end; ++k, ++it) {
+          const uint32_t s = it % STAGES, ph = (it / STAGES) & 1u;
+          if (!wait_phase<false>(empty_bar(s), ph ^ 1u, abort_flag, p, B2G_SITE_EMPTY)) {
+            alive = false;
+            break;
+          }
+          if (leader) mbar_arrive_expect_tx(full_bar(s), SP::kTxBytes);
+          const uint32_t fb = CG == 1 ? full_bar(s) : map_to_cta(full_bar(s), 0);
+          const int32_t kx = k * 128;
+          const uint32_t a_dst = sbase + SP::kAOff + s * SP::kABytes;
+          const uint32_t b_dst = sbase + SP::kBOff + s * SP::kBBytes;
+          if constexpr (CG == 1) {
+            tma_load_2d(a_dst, &p.tmA, fb, kx, a_row);
+            tma_load_2d(b_dst, &p.tmB, fb, kx, b_row);
+          } else {
+            tma_load_2d_pair(a_dst, &p.tmA, fb, kx, a_row);
+            tma_load_2d_pair(b_dst, &p.tmB, fb, kx, b_row);
+          }
+          if constexpr (kScaled) {
+            static_assert(CG == 1, "block-scaled kinds run with cta_group::1");
+            const uint32_t sfa_dst = sbase + SP::kSfaOff + s * SP::kSfaBytes;
+            const uint32_t sfb_dst = sbase + SP::kSfbOff + s * SP::kSfbBytes;
+            const size_t g0 = static_cast<size_t>(k) * kGps;
+            const uint8_t* sa =
+                p.sfa + (static_cast<size_t>(a_row >> 7) * p.sf_groups + g0) * 512u;
+            bulk_load(sfa_dst, sa, kGps * 512u, fb);
+#pragma unroll
+            for (int rb = 0; rb < 2; ++rb) {
+              const uint8_t* sb =
+                  p.sfb + (static_cast<size_t>(w.tn * 2 + rb) * p.sf_groups + g0) * 512u;
+              bulk_load(sfb_dst + rb * kGps * 512u, sb, kGps * 512u, fb);
+            }
+          }
+        }
+      }
+      // Drain: every load issued must have landed before the CTA can exit.
+      if (leader) {
+        const uint32_t first = it > STAGES ? it - STAGES : 0u;
+        for (uint32_t i = first; i < it; ++i) {
+          const uint32_t s = i % STAGES, ph = (i / STAGES) & 1u;
+          uint32_t spins = 0;
+          while (!mbar_try_wait(full_bar(s), ph) && spins < (1u << 20)) ++spins;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ----------------------------------------------------------- MMA issue --
+    if (leader && lane == 0) {
+      uint32_t it = 0, tcount = 0;
+      WorkCursor cur = cursor_begin(p.plan, unit);
+      WorkItem w;
+      bool alive = true;
+      while (alive && cursor_next(p.plan, unit, cur, w)) {
+        const uint32_t b = tcount & 1u, aph = (tcount >> 1) & 1u;
+        if (!wait_phase<CG == 2>(acce_bar(b), aph ^ 1u, abort_flag, p, B2G_SITE_ACC_EMPTY)) break;
+        if constexpr (kScaled) {
+          if (tcount > 0 &&
+              !wait_phase<CG == 2>(ovl_bar, (tcount - 1) & 1u, abort_flag, p, B2G_SITE_OVERLAP))
+            break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + b * SP::kAccStride;
+        for (int32_t k = w.k_begin; k < w.k_end; ++k, ++it) {
+          const uint32_t s = it % STAGES, ph = (it / STAGES) & 1u;
+          if (!wait_phase<false>(full_bar(s), ph, abort_flag, p, B2G_SITE_FULL)) {
+            alive = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = sbase + SP::kAOff + s * SP::kABytes;
+          const uint32_t b_addr = sbase + SP::kBOff + s * SP::kBBytes;
+          const uint64_t adesc = sdesc_kmajor_sw128(a_addr);
+          const uint64_t bdesc = sdesc_kmajor_sw128(b_addr);
+          if constexpr (kScaled) {
+            const uint32_t sfa_addr = sbase + SP::kSfaOff + s * SP::kSfaBytes;
+            const uint32_t sfb_addr = sbase + SP::kSfbOff + s * SP::kSfbBytes;
+#pragma unroll
+            for (int g = 0; g < kGps; ++g) {
+              tmem_cp_32x128b_x4<CG>(tmem_base + SP::kSfaCol + 4 * g,
+                                     sdesc_rows16(sfa_addr + g * 512));
+#pragma unroll
+              for (int rb = 0; rb < 2; ++rb)
+                tmem_cp_32x128b_x4<CG>(tmem_base + SP::kSfbCol + 8 * g + 4 * rb,
+                                       sdesc_rows16(sfb_addr + (rb * kGps + g) * 512));
+            }
+          }
+#pragma unroll
+          for (uint32_t j = 0; j < 4; ++j) {
+            // +32 bytes of K per MMA inside the 128-byte swizzled row
+            const uint64_t ad = adesc + 2u * j;
+            const uint64_t bd = bdesc + 2u * j;
+            const uint32_t acc = (k > w.k_begin || j > 0) ? 1u : 0u;
+            if constexpr (KIND == kKindF16 || KIND == kKindBF16) {
+              mma_f16<CG>(d_tmem, ad, bd, make_idesc<KIND, CG>(0), acc);
+            } else if constexpr (KIND == kKindE5M2) {
+              mma_f8f6f4<CG>(d_tmem, ad, bd, make_idesc<KIND, CG>(0), acc);
+            } else {
+              const uint32_t g = KIND == kKindMXFP4 ? (j >> 1) : 0u;
+              const uint32_t sf_id = KIND == kKindMXFP4 ? ((j & 1u) * 2u) : j;
+              const uint32_t sfa_t = (tmem_base + SP::kSfaCol + 4 * g) | (sf_id << 30);
+              const uint32_t sfb_t = (tmem_base + SP::kSfbCol + 8 * g) | (sf_id << 30);
+              if constexpr (KIND == kKindMXFP4)
+                mma_mxf4<CG>(d_tmem, ad, bd, make_idesc<KIND, CG>(sf_id), sfa_t, sfb_t, acc);
+              else
+                mma_mxf8f6f4<CG>(d_tmem, ad, bd, make_idesc<KIND, CG>(sf_id), sfa_t, sfb_t, acc);
+            }
+          }
+          if constexpr (CG == 1)
+            tc_commit<1>(empty_bar(s));
+          else
+            tc_commit_pair(empty_bar(s), 0x3);
+        }
+        if (!alive) break;
+        if constexpr (CG == 1)
+          tc_commit<1>(accf_bar(b));
+        else
+          tc_commit_pair(accf_bar(b), 0x3);
+        ++tcount;
+      }
+      // Drain: all MMAs / copies issued by this thread complete before TMEM is freed.
+      tc_commit<CG>(drain_bar);
+      uint32_t spins = 0;
+      while (!mbar_try_wait(drain_bar, 0) && spins < (1u << 22)) ++spins;
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue --
+    const uint32_t quad = warp & 3u;
+    const uint32_t row = quad * 32u + lane;  // accumulator row inside the CTA
+    uint8_t* stage_base = smem + SP::kEpiOff + (warp - 2) * SP::kEpiBufs * SP::kEpiBufBytes;
+    uint32_t tcount = 0, nstore = 0;
+    WorkCursor cur = cursor_begin(p.plan, unit);
+    WorkItem w;
+    while (cursor_next(p.plan, unit, cur, w)) {
+      const uint32_t b = tcount & 1u, aph = (tcount >> 1) & 1u;
+      const bool ok = wait_phase<false>(accf_bar(b), aph, abort_flag, p, B2G_SITE_ACC_FULL);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + ((quad * 32u) << 16) + b * SP::kAccStride;
+      const int32_t m0 = w.tm * (128 * CG) + static_cast<int32_t>(rank) * 128 + quad * 32;
+      const int32_t n0 = w.tn * 256;
+      const uint32_t first_chunk = kScaled ? (b == 0 ? 7u : 0u) : 0u;
+      bool contribs_ready = w.role != kRoleOwner;
+      bool failed = false;
+#pragma unroll 1
+      for (uint32_t ci = 0; ci < 8; ++ci) {
+        const uint32_t c = (first_chunk + ci) & 7u;
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tbase + c * 32u, v);
+        tmem_wait_ld();
+        if constexpr (kScaled) {
+          if (ci == 0) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+              if constexpr (CG == 1)
+                mbar_arrive(ovl_bar);
+              else
+                mbar_arrive_remote(map_to_cta(ovl_bar, 0));
+            }
+          }
+        }
+        if (w.role == kRoleContrib) {
+          float4* dst = reinterpret_cast<float4*>(p.partials + partial_slot(unit, rank, CG) +
+                                                  static_cast<size_t>(row) * 256u + c * 32u);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            __stcg(dst + i, make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                                        __uint_as_float(v[4 * i + 2]),
+                                        __uint_as_float(v[4 * i + 3])));
+          continue;
+        }
+        if (w.role == kRoleOwner) {
+          if (!contribs_ready) {
+            bool fok = true;
+            for (int32_t u2 = w.first_contrib; u2 <= w.last_contrib && fok; ++u2)
+              fok = wait_flag(p.flags + flag_index(u2, rank, quad, CG), p.inject ? 2u : 1u,
+                              abort_flag, p, B2G_SITE_FLAG);
+            fok = __all_sync(0xffffffffu, fok);
+            if (!fok) {
+              failed = true;
+              break;
+            }
+            contribs_ready = true;
+          }
+          for (int32_t u2 = w.first_contrib; u2 <= w.last_contrib; ++u2) {
+            const float4* src = reinterpret_cast<const float4*>(
+                p.partials + partial_slot(u2, rank, CG) + static_cast<size_t>(row) * 256u +
+                c * 32u);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float4 t = __ldcg(src + i);
+              v[4 * i + 0] = __float_as_uint(__uint_as_float(v[4 * i + 0]) + t.x);
+              v[4 * i + 1] = __float_as_uint(__uint_as_float(v[4 * i + 1]) + t.y);
+              v[4 * i + 2] = __float_as_uint(__uint_as_float(v[4 * i + 2]) + t.z);
+              v[4 * i + 3] = __float_as_uint(__uint_as_float(v[4 * i + 3]) + t.w);
+            }
+          }
+        }
+        // Convert and stage 32 rows x 32 columns in the 64-byte swizzle.
+        uint8_t* buf = stage_base + (nstore & 1u) * SP::kEpiBufBytes;
+        if (lane == 0) bulk_wait_group_read<1>();
+        __syncwarp();
+#pragma unroll
+        for (uint32_t pc = 0; pc < 4; ++pc) {
+          uint4 q4;
+          q4.x = pack_out<OUT_BF16>(v[8 * pc + 0], v[8 * pc + 1]);
+          q4.y = pack_out<OUT_BF16>(v[8 * pc + 2], v[8 * pc + 3]);
+          q4.z = pack_out<OUT_BF16>(v[8 * pc + 4], v[8 * pc + 5]);
+          q4.w = pack_out<OUT_BF16>(v[8 * pc + 6], v[8 * pc + 7]);
+          const uint32_t off = lane * 64u + ((pc ^ ((lane >> 1) & 3u)) << 4);
+          *reinterpret_cast<uint4*>(buf + off) = q4;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        const int32_t x = n0 + static_cast<int32_t>(c * 32u);
+        if (lane == 0 && x < p.N && m0 < p.M) {
+          tma_store_2d(&p.tmC, smem_u32(buf), x, m0);
+          bulk_commit_group();
+        }
+        ++nstore;
+      }
+      if (failed) break;
+      if (w.role == kRoleContrib) {
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) st_release_gpu(p.flags + flag_index(unit, rank, quad, CG), 1u);
+      } else if (w.role == kRoleOwner) {
+        __syncwarp();
+        if (lane == 0)
+          for (int32_t u2 = w.first_contrib; u2 <= w.last_contrib; ++u2)
+            p.flags[flag_index(u2, rank, quad, CG)] = 0u;
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if constexpr (CG == 1)
+          mbar_arrive(acce_bar(b));
+        else
+          mbar_arrive_remote(map_to_cta(acce_bar(b), 0));
+      }
+      ++tcount;
+    }
+    if (lane == 0) bulk_wait_group<0>();
+    __syncwarp();
+  }
+
+  // ------------------------------------------------------------- teardown --
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if constexpr (CG == 2) cluster_arrive_wait();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc<CG>(tmem_base, 512);
+  }
+}
+
+}  // namespace b2g

@@ -1,0 +1,155 @@
+// Persistent tile scheduler: data-parallel full tiles, then a stream-K
+// remainder. Shared by the host (planning, workspace sizing, CPU tests of the
+// partition) and the device (every role of every CTA walks the same list).
+//
+// Replaces the reference's one-program-per-tile grid and its tile raster
+// (kernels/gemm/utils/common.py:38-83 get_pids: XCD remap + GROUP_SIZE_M
+// swizzle). On B200 the grid is one work unit per SM (cta_group::1) or per SM
+// pair (cta_group::2); a unit walks its tiles in the same GROUP_M-swizzled
+// raster so concurrently running units share A and B panels in L2.
+//
+// Stream-K ownership rule: the unit that runs k-iteration 0 of a split tile
+// owns it. Every other unit touching the tile does so in the FIRST segment of
+// its range, writes an fp32 partial to its own workspace slot and raises a
+// flag; the owner adds the partials in increasing unit order (deterministic)
+// after its own accumulation and stores C. Contributors never wait, so the
+// waits cannot form a cycle.
+#pragma once
+
+#include <stdint.h>
+
+#if defined(__CUDACC__)
+#define B2G_HD __host__ __device__ __forceinline__
+#else
+#define B2G_HD inline
+#endif
+
+namespace b2g {
+
+enum : int { kRoleFull = 0, kRoleOwner = 1, kRoleContrib = 2 };
+
+struct SkPlan {
+  int32_t tiles_m, tiles_n;  // output tile grid
+  int32_t k_iters;           // k-iterations (pipeline stages) per tile
+  int32_t units;             // persistent work units launched
+  int32_t dp_tiles;          // tiles [0, dp_tiles) are data-parallel
+  int32_t sk_units;          // units [0, sk_units) share the stream-K iterations
+  int64_t sk_iters;          // (tiles - dp_tiles) * k_iters
+  int32_t group_m;           // raster group height in tiles
+};
+
+struct WorkItem {
+  int32_t tile;      // raster index
+  int32_t tm, tn;    // tile coordinates
+  int32_t k_begin;   // first k-iteration (inclusive)
+  int32_t k_end;     // last k-iteration (exclusive)
+  int32_t role;      // kRoleFull / kRoleOwner / kRoleContrib
+  int32_t first_contrib, last_contrib;  // owner only: contributing units [first, last]
+};
+
+B2G_HD int32_t plan_tiles(const SkPlan& p) { return p.tiles_m * p.tiles_n; }
+
+B2G_HD void tile_coords(const SkPlan& p, int32_t t, int32_t& tm, int32_t& tn) {
+  const int32_t per_group = p.group_m * p.tiles_n;
+  const int32_t g = t / per_group;
+  const int32_t first_m = g * p.group_m;
+  int32_t gm = p.tiles_m - first_m;
+  if (gm > p.group_m) gm = p.group_m;
+  const int32_t r = t - g * per_group;
+  tm = first_m + r % gm;
+  tn = r / gm;
+}
+
+B2G_HD int64_t sk_range_begin(const SkPlan& p, int32_t u) {
+  return (p.sk_iters * u) / p.sk_units;
+}
+
+// Builds the plan. `sk_mode`: 0 = no stream-K (all tiles data-parallel, the
+// last wave partial); 1 = stream-K over the partial last wave only;
+// 2 = stream-K over the last full wave plus the partial one.
+inline SkPlan make_plan(int32_t tiles_m, int32_t tiles_n, int32_t k_iters, int32_t units,
+                        int32_t group_m, int32_t sk_mode, int32_t min_sk_iters) {
+  SkPlan p{};
+  p.tiles_m = tiles_m;
+  p.tiles_n = tiles_n;
+  p.k_iters = k_iters;
+  p.units = units;
+  p.group_m = group_m < 1 ? 1 : group_m;
+  const int32_t tiles = tiles_m * tiles_n;
+  int32_t dp = tiles;
+  if (sk_mode != 0 && tiles % units != 0) {
+    int32_t waves = tiles / units;
+    if (sk_mode == 2 && waves >= 1) waves -= 1;
+    dp = waves * units;
+  }
+  p.dp_tiles = dp;
+  p.sk_iters = static_cast<int64_t>(tiles - dp) * k_iters;
+  if (p.sk_iters > 0) {
+    if (min_sk_iters < 1) min_sk_iters = 1;
+    int64_t su = p.sk_iters / min_sk_iters;
+    if (su > units) su = units;
+    if (su < 1) su = 1;
+    p.sk_units = static_cast<int32_t>(su);
+  } else {
+    p.sk_units = 0;
+  }
+  return p;
+}
+
+// Iterates the work items of unit `u` in execution order.
+struct WorkCursor {
+  int32_t dp_next;   // next data-parallel tile index
+  int64_t sk_pos;    // next stream-K iteration
+  int64_t sk_end;    // end of this unit's stream-K range
+};
+
+B2G_HD WorkCursor cursor_begin(const SkPlan& p, int32_t u) {
+  WorkCursor c;
+  c.dp_next = u;
+  if (u < p.sk_units) {
+    c.sk_pos = sk_range_begin(p, u);
+    c.sk_end = sk_range_begin(p, u + 1);
+  } else {
+    c.sk_pos = 0;
+    c.sk_end = 0;
+  }
+  return c;
+}
+
+B2G_HD bool cursor_next(const SkPlan& p, int32_t u, WorkCursor& c, WorkItem& w) {
+  if (c.dp_next < p.dp_tiles) {
+    w.tile = c.dp_next;
+    w.k_begin = 0;
+    w.k_end = p.k_iters;
+    w.role = kRoleFull;
+    w.first_contrib = w.last_contrib = -1;
+    c.dp_next += p.units;
+    tile_coords(p, w.tile, w.tm, w.tn);
+    return true;
+  }
+  if (c.sk_pos >= c.sk_end) return false;
+  const int64_t local_tile = c.sk_pos / p.k_iters;
+  const int64_t tile_begin = local_tile * p.k_iters;
+  const int64_t tile_end = tile_begin + p.k_iters;
+  const int64_t seg_end = c.sk_end < tile_end ? c.sk_end : tile_end;
+  w.tile = p.dp_tiles + static_cast<int32_t>(local_tile);
+  w.k_begin = static_cast<int32_t>(c.sk_pos - tile_begin);
+  w.k_end = static_cast<int32_t>(seg_end - tile_begin);
+  w.first_contrib = w.last_contrib = -1;
+  if (w.k_begin > 0) {
+    w.role = kRoleContrib;
+  } else if (w.k_end == p.k_iters) {
+    w.role = kRoleFull;
+  } else {
+    w.role = kRoleOwner;
+    int32_t v = u + 1;
+    w.first_contrib = v;
+    while (v < p.sk_units && sk_range_begin(p, v) < tile_end) ++v;
+    w.last_contrib = v - 1;
+  }
+  c.sk_pos = seg_end;
+  tile_coords(p, w.tile, w.tm, w.tn);
+  return true;
+}
+
+}  // namespace b2g

@@ -1,0 +1,301 @@
+"""Torch-facing calls into libb2g.so.
+
+Every function launches asynchronously on the current torch CUDA stream and
+returns without synchronising, as the reference's ``matmul`` wrappers do
+(kernels/gemm/intra_wave/a16w16/v9_beyond_hotloop/matmul_kernel.py:390-424).
+Tensors only provide device pointers, strides and the stream; the work is done
+by the sm_100a kernels behind the C ABI.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+
+import torch
+
+from . import _lib
+from ._lib import B2GError, check, lib
+
+_OUT_DT = {torch.float16: _lib.DT_F16, torch.bfloat16: _lib.DT_BF16}
+_IN_DT = {torch.float16: _lib.DT_F16, torch.bfloat16: _lib.DT_BF16, torch.float32: _lib.DT_F32}
+
+_ws_lock = threading.Lock()
+_workspaces: dict[tuple[int, int], torch.Tensor] = {}
+_status: dict[int, torch.Tensor] = {}
+
+
+def _stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(*ts: torch.Tensor) -> torch.device:
+    dev = ts[0].device
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise ValueError("b2g kernels take CUDA tensors (there is no CPU path)")
+        if t.device != dev:
+            raise ValueError("all operands must be on the same device")
+    return dev
+
+
+def workspace(nbytes: int, device: torch.device) -> torch.Tensor:
+    """Zero-initialised scratch of at least ``nbytes`` for (device, current stream).
+
+    The kernels leave it zeroed after a successful run, so it is reused as is.
+    """
+    key = (device.index, _stream_handle(device))
+    with _ws_lock:
+        ws = _workspaces.get(key)
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
+            _workspaces[key] = ws
+        return ws
+
+
+def status_tensor(device: torch.device) -> torch.Tensor:
+    """The device status word that kernels on ``device`` report bounded-wait timeouts in."""
+    with _ws_lock:
+        st = _status.get(device.index)
+        if st is None:
+            st = torch.zeros(1, dtype=torch.int32, device=device)
+            _status[device.index] = st
+        return st
+
+
+def check_status(device: torch.device | None = None, reset: bool = True) -> None:
+    """Synchronises ``device`` and raises B2GError if a kernel set the status word.
+
+    After a timeout the stream-K flags in the workspaces may be stale, so they are
+    cleared before raising.
+    """
+    device = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+    st = status_tensor(device)
+    code = int(st.item())
+    if code != 0:
+        with _ws_lock:
+            for (idx, _), ws in _workspaces.items():
+                if idx == device.index:
+                    ws.zero_()
+        if reset:
+            st.zero_()
+        torch.cuda.synchronize(device)
+        raise B2GError(code, "kernel status")
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _k_major(t: torch.Tensor) -> torch.Tensor:
+    """A view (or copy) with unit stride along the last dim, 16-byte row stride and base."""
+    eb = t.element_size()
+    ok = (t.dim() == 2 and t.stride(1) == 1 and (t.stride(0) * eb) % 16 == 0
+          and t.stride(0) >= t.shape[1] and t.data_ptr() % 16 == 0)
+    if ok:
+        return t
+    rows, cols = t.shape
+    pad = (-cols * eb) % 16 // eb
+    out = torch.zeros((rows, cols + pad), dtype=t.dtype, device=t.device)
+    out[:, :cols].copy_(t)
+    return out[:, :cols]
+
+
+def _out(c: torch.Tensor | None, M: int, N: int, dtype: torch.dtype, device) -> torch.Tensor:
+    if c is None:
+        c = torch.empty((M, N), dtype=dtype, device=device)
+    if c.shape != (M, N) or c.dtype not in _OUT_DT:
+        raise ValueError(f"c must be ({M}, {N}) fp16/bf16, got {tuple(c.shape)} {c.dtype}")
+    return c
+
+
+def _c_view(c: torch.Tensor) -> tuple[torch.Tensor, bool]:
+    """Returns an output buffer the kernel can store into and whether to copy back."""
+    eb = c.element_size()
+    if c.stride(1) == 1 and (c.stride(0) * eb) % 16 == 0 and c.data_ptr() % 16 == 0:
+        return c, False
+    return _k_major(torch.empty_like(c)), True
+
+
+def gemm_f16(a: torch.Tensor, b_t: torch.Tensor, c: torch.Tensor | None = None,
+             out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """C = A @ B_t^T for fp16/bf16 A (M, K) and B_t (N, K); C (M, N) fp16/bf16."""
+    dev = _require_cuda(a, b_t)
+    if a.dtype not in (torch.float16, torch.bfloat16) or b_t.dtype != a.dtype:
+        raise ValueError(f"a16w16 takes two fp16 or two bf16 operands, got {a.dtype}, {b_t.dtype}")
+    M, K = a.shape
+    N, K2 = b_t.shape
+    if K != K2:
+        raise ValueError("Incompatible dimensions")
+    c = _out(c, M, N, out_dtype or (c.dtype if c is not None else a.dtype), dev)
+    a_, b_ = _k_major(a), _k_major(b_t)
+    cv, copy_back = _c_view(c)
+    nbytes = lib().b2g_gemm_workspace_bytes(
+        _lib.KIND_F16 if a.dtype == torch.float16 else _lib.KIND_BF16, M, N, K)
+    ws = workspace(nbytes, dev)
+    rc = lib().b2g_gemm_f16(a_.data_ptr(), a_.stride(0), b_.data_ptr(), b_.stride(0),
+                            cv.data_ptr(), cv.stride(0), M, N, K, _IN_DT[a.dtype],
+                            _OUT_DT[c.dtype], ws.data_ptr(), ws.numel(),
+                            status_tensor(dev).data_ptr(), _stream_handle(dev))
+    check(rc, "b2g_gemm_f16")
+    if copy_back:
+        c.copy_(cv)
+    return c
+
+
+def _as_bytes(t: torch.Tensor) -> torch.Tensor:
+    return t if t.dtype == torch.uint8 else t.view(torch.uint8)
+
+
+def gemm_f8(a: torch.Tensor, b_t: torch.Tensor, c: torch.Tensor | None = None,
+            a_scales: torch.Tensor | None = None, b_scales: torch.Tensor | None = None,
+            out_dtype: torch.dtype = torch.float16) -> torch.Tensor:
+    """C = A @ B_t^T for e5m2 A (M, K), B_t (N, K), optionally with E8M0 scales
+    a_scales (M, K/32) and b_scales (N, K/32) of any strides."""
+    dev = _require_cuda(a, b_t)
+    for t in (a, b_t):
+        if t.dtype not in (torch.float8_e5m2, torch.uint8):
+            raise ValueError(f"a8w8 takes float8_e5m2 (or raw uint8) operands, got {t.dtype}")
+    if (a_scales is None) != (b_scales is None):
+        raise ValueError("give both scale tensors or neither")
+    M, K = a.shape
+    N, K2 = b_t.shape
+    if K != K2:
+        raise ValueError("Incompatible dimensions")
+    c = _out(c, M, N, c.dtype if c is not None else out_dtype, dev)
+    a_, b_ = _k_major(_as_bytes(a)), _k_major(_as_bytes(b_t))
+    cv, copy_back = _c_view(c)
+    scaled = a_scales is not None
+    kind = _lib.KIND_MXE5M2 if scaled else _lib.KIND_E5M2
+    if scaled:
+        _check_scales(a_scales, M, K, "a_scales")
+        _check_scales(b_scales, N, K, "b_scales")
+    ws = workspace(lib().b2g_gemm_workspace_bytes(kind, M, N, K), dev)
+    rc = lib().b2g_gemm_f8(
+        a_.data_ptr(), a_.stride(0), b_.data_ptr(), b_.stride(0),
+        _ptr(a_scales), a_scales.stride(0) if scaled else 0, a_scales.stride(1) if scaled else 0,
+        _ptr(b_scales), b_scales.stride(0) if scaled else 0, b_scales.stride(1) if scaled else 0,
+        cv.data_ptr(), cv.stride(0), M, N, K, _OUT_DT[c.dtype], ws.data_ptr(), ws.numel(),
+        status_tensor(dev).data_ptr(), _stream_handle(dev))
+    check(rc, "b2g_gemm_f8")
+    if copy_back:
+        c.copy_(cv)
+    return c
+
+
+def _check_scales(s: torch.Tensor, rows: int, K: int, name: str) -> None:
+    if s.dtype != torch.uint8 or not s.is_cuda:
+        raise ValueError(f"{name} must be a CUDA uint8 (E8M0) tensor")
+    if tuple(s.shape) != (rows, K // 32):
+        raise ValueError(f"{name} must have shape ({rows}, {K // 32}), got {tuple(s.shape)}")
+
+
+def gemm_mxf4(a: torch.Tensor, b_t: torch.Tensor, a_scales: torch.Tensor,
+              b_scales: torch.Tensor, c: torch.Tensor | None = None,
+              out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """C = dequant(A) @ dequant(B_t)^T for packed e2m1 A (M, K/2), B_t (N, K/2)
+    and E8M0 scales a_scales (M, K/32), b_scales (N, K/32) of any strides."""
+    dev = _require_cuda(a, b_t, a_scales, b_scales)
+    if a.dtype != torch.uint8 or b_t.dtype != torch.uint8:
+        raise ValueError("a4w4 operands are packed uint8")
+    M, Kp = a.shape
+    N, Kp2 = b_t.shape
+    if Kp != Kp2:
+        raise ValueError("Incompatible dimensions")
+    K = 2 * Kp
+    _check_scales(a_scales, M, K, "a_scales")
+    _check_scales(b_scales, N, K, "b_scales")
+    c = _out(c, M, N, c.dtype if c is not None else out_dtype, dev)
+    a_, b_ = _k_major(a), _k_major(b_t)
+    cv, copy_back = _c_view(c)
+    ws = workspace(lib().b2g_gemm_workspace_bytes(_lib.KIND_MXFP4, M, N, K), dev)
+    rc = lib().b2g_gemm_mxf4(
+        a_.data_ptr(), a_.stride(0), b_.data_ptr(), b_.stride(0),
+        a_scales.data_ptr(), a_scales.stride(0), a_scales.stride(1),
+        b_scales.data_ptr(), b_scales.stride(0), b_scales.stride(1),
+        cv.data_ptr(), cv.stride(0), M, N, K, _OUT_DT[c.dtype], ws.data_ptr(), ws.numel(),
+        status_tensor(dev).data_ptr(), _stream_handle(dev))
+    check(rc, "b2g_gemm_mxf4")
+    if copy_back:
+        c.copy_(cv)
+    return c
+
+
+# ------------------------------------------------------------------ packing --
+def quantize_mxfp4(x: torch.Tensor, rows_pad: int | None = None
+                   ) -> tuple[torch.Tensor, torch.Tensor]:
+    """fp32 (rows, K) -> (packed e2m1 (rows, K/2) uint8, E8M0 scales (rows, K/32)).
+
+    The scales are returned as the reference stores them: a (K/32, rows_pad)
+    M-contiguous buffer viewed transposed, strides (1, rows_pad)
+    (kernels/gemm/intra_wave/a4w4/bench.py:138-144).
+    """
+    dev = _require_cuda(x)
+    if x.dtype != torch.float32 or x.dim() != 2:
+        raise ValueError("quantize_mxfp4 takes a 2-D fp32 tensor")
+    x = _k_major(x)
+    rows, K = x.shape
+    rows_pad = rows_pad or rows
+    q = torch.empty((rows, K // 2), dtype=torch.uint8, device=dev)
+    sc_store = torch.empty((K // 32, rows_pad), dtype=torch.uint8, device=dev)
+    sc = sc_store.T[:rows]
+    rc = lib().b2g_quant_mxfp4(x.data_ptr(), x.stride(0), rows, K, q.data_ptr(), q.stride(0),
+                               sc.data_ptr(), sc.stride(0), sc.stride(1), _stream_handle(dev))
+    check(rc, "b2g_quant_mxfp4")
+    return q, sc
+
+
+def quantize_mxe5m2(x: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    """fp32 (rows, K) with given E8M0 scales (rows, K/32) -> e5m2 (rows, K)."""
+    dev = _require_cuda(x, scales)
+    if x.dtype != torch.float32 or x.dim() != 2:
+        raise ValueError("quantize_mxe5m2 takes a 2-D fp32 tensor")
+    x = _k_major(x)
+    rows, K = x.shape
+    _check_scales(scales, rows, K, "scales")
+    q = torch.empty((rows, K), dtype=torch.uint8, device=dev)
+    rc = lib().b2g_quant_mxe5m2(x.data_ptr(), x.stride(0), rows, K, scales.data_ptr(),
+                                scales.stride(0), scales.stride(1), q.data_ptr(), q.stride(0),
+                                _stream_handle(dev))
+    check(rc, "b2g_quant_mxe5m2")
+    return q.view(torch.float8_e5m2)
+
+
+def cast_e5m2(x: torch.Tensor) -> torch.Tensor:
+    """Elementwise fp16/bf16/fp32 -> float8_e5m2 with torch's rounding."""
+    dev = _require_cuda(x)
+    if x.dtype not in _IN_DT:
+        raise ValueError(f"cast_e5m2 takes fp16/bf16/fp32, got {x.dtype}")
+    xc = x.contiguous()
+    out = torch.empty(x.shape, dtype=torch.uint8, device=dev)
+    rc = lib().b2g_cast_e5m2(xc.data_ptr(), _IN_DT[x.dtype], xc.numel(), out.data_ptr(),
+                             _stream_handle(dev))
+    check(rc, "b2g_cast_e5m2")
+    return out.view(torch.float8_e5m2)
+
+
+def plan(kind: int, M: int, N: int, K: int, num_sms: int = 148) -> dict:
+    """Host-side schedule summary (no GPU needed)."""
+    out = (ctypes.c_int32 * 9)()
+    check(lib().b2g_plan_query(kind, M, N, K, num_sms, out, 9), "b2g_plan_query")
+    keys = ("cta_group", "tiles_m", "tiles_n", "k_iters", "units", "dp_tiles", "sk_units",
+            "launched", "group_m")
+    return dict(zip(keys, list(out)))
+
+
+def plan_items(kind: int, M: int, N: int, K: int, unit: int, num_sms: int = 148) -> list[tuple]:
+    """Work items (tile, tm, tn, k_begin, k_end, role, first, last) of one unit."""
+    n = lib().b2g_plan_items(kind, M, N, K, num_sms, unit, None, 0)
+    if n < 0:
+        check(n, "b2g_plan_items")
+    buf = (ctypes.c_int32 * (8 * max(n, 1)))()
+    lib().b2g_plan_items(kind, M, N, K, num_sms, unit, buf, n)
+    return [tuple(buf[8 * i:8 * i + 8]) for i in range(n)]
+
+
+__all__ = [
+    "B2GError", "gemm_f16", "gemm_f8", "gemm_mxf4", "quantize_mxfp4", "quantize_mxe5m2",
+    "cast_e5m2", "workspace", "status_tensor", "check_status", "plan", "plan_items",
+]

@@ -1,0 +1,178 @@
+/*
+ * b2g.h - C ABI of the B200 (sm_100a) GEMM hot path: C = A * B^T in
+ * FP16/BF16 (a16w16), BF8 = E5M2 (a8w8, unscaled or with E8M0 per-32-K scales)
+ * and MXFP4 = packed E2M1 with E8M0 per-32-K scales (a4w4), plus the
+ * quantise-and-pack kernels that produce the low-precision operands.
+ *
+ * Conventions (all entry points):
+ *   - Plain device pointers, element strides in elements of the operand's own
+ *     storage type (bytes for e5m2, packed e2m1 and E8M0 scales), `stream` is a
+ *     cudaStream_t passed as void*.
+ *   - A is M x K and B is N x K, both K-contiguous (row stride lda / ldb);
+ *     C is M x N row-major with row stride ldc. This is the layout the
+ *     reference's kernels see when its bench passes `b` as a (K, N) view of an
+ *     (N, K) K-contiguous tensor.
+ *   - Launches are asynchronous on `stream`. Nothing synchronises.
+ *   - Return value: 0 on success, a negative B2G_E* code when an argument is
+ *     rejected before launch (nothing was launched), or a positive CUDA error.
+ *   - `status` (nullable) is a device int the kernel sets to a nonzero
+ *     B2G_STATUS_* code when a bounded wait expired. Zero it before use; read
+ *     it after synchronising. After a nonzero status the workspace flags may be
+ *     stale: clear the workspace with b2g_workspace_reset before reuse.
+ *   - `workspace` is caller-owned device memory of at least
+ *     b2g_gemm_workspace_bytes(...) bytes, zeroed once when allocated
+ *     (b2g_workspace_reset). The kernels leave it zeroed after a successful
+ *     run. Calls that share a workspace must not overlap on the GPU.
+ *
+ * Reference interfaces replaced (paths inside jamesbowley/gfx950-gluon-tutorials):
+ *   a16w16 matmul(a, b, c=None)
+ *       kernels/gemm/intra_wave/a16w16/v9_beyond_hotloop/matmul_kernel.py:390-424
+ *       kernels/gemm/inter_wave/a16w16/matmul_kernel.py:335-379 (matmul_kernel_only)
+ *   a8w8 matmul(a, b)
+ *       kernels/gemm/intra_wave/a8w8/matmul_kernel.py:437-470
+ *       kernels/gemm/inter_wave/a8w8/matmul_kernel.py:343-388
+ *   a4w4 matmul(a, b, a_scales, b_scales)
+ *       kernels/gemm/intra_wave/a4w4/v1_sliceMN/matmul_kernel.py:696-742
+ *       kernels/gemm/inter_wave/a4w4/v2_mfma32x32x64/matmul_kernel.py:614-668
+ */
+#ifndef B2G_H_
+#define B2G_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(B2G_EXPORT) && defined(__GNUC__)
+#define B2G_API __attribute__((visibility("default")))
+#else
+#define B2G_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- operand kinds (b2g_gemm_workspace_bytes `kind`) ---- */
+#define B2G_KIND_F16 0    /* fp16 x fp16, kind::f16 */
+#define B2G_KIND_BF16 1   /* bf16 x bf16, kind::f16 */
+#define B2G_KIND_E5M2 2   /* e5m2 x e5m2, no scales, kind::f8f6f4 */
+#define B2G_KIND_MXE5M2 3 /* e5m2 x e5m2 with E8M0 per 32 K, kind::mxf8f6f4 */
+#define B2G_KIND_MXFP4 4  /* packed e2m1 x e2m1 with E8M0 per 32 K, kind::mxf4 */
+
+/* ---- element types ---- */
+#define B2G_DT_F16 0
+#define B2G_DT_BF16 1
+#define B2G_DT_F32 2
+
+/* ---- argument errors (returned before any launch) ---- */
+#define B2G_OK 0
+#define B2G_EINVAL -1        /* bad kind / dtype / null pointer */
+#define B2G_ESHAPE -2        /* M, N or K out of range or K not a multiple of the kind's unit */
+#define B2G_EALIGN -3        /* pointer or row stride not 16-byte aligned */
+#define B2G_ESTRIDE -4       /* operand not K-contiguous / overlapping rows */
+#define B2G_EWORKSPACE -5    /* workspace missing or too small */
+#define B2G_ETENSORMAP -6    /* the driver refused a TMA descriptor */
+#define B2G_ENODEVICE -7     /* no sm_100 device current */
+#define B2G_ECAPACITY -8     /* a size exceeds a fixed capacity of the entry point */
+
+/* ---- device status word codes (set by kernels, read by the caller) ---- */
+#define B2G_STATUS_TIMEOUT 0x1000 /* a bounded wait expired; low byte = wait site */
+#define B2G_SITE_EMPTY 1          /* producer waiting for a free ring slot */
+#define B2G_SITE_FULL 2           /* MMA waiting for a filled ring slot */
+#define B2G_SITE_ACC_EMPTY 3      /* MMA waiting for a drained accumulator */
+#define B2G_SITE_ACC_FULL 4       /* epilogue waiting for a finished accumulator */
+#define B2G_SITE_OVERLAP 5        /* MMA waiting for the shared accumulator columns */
+#define B2G_SITE_FLAG 6           /* stream-K owner waiting for a contributor */
+
+/* Library ABI version (major * 100 + minor). */
+B2G_API int b2g_version(void);
+
+/* Human-readable text for a return code or a status word. */
+B2G_API const char* b2g_strerror(int code);
+
+/* Bytes of workspace the GEMM entry points need on the current device. */
+B2G_API size_t b2g_gemm_workspace_bytes(int kind, int M, int N, int K);
+
+/* Zero `bytes` of workspace on `stream` (once after allocation, and after a
+ * nonzero status). */
+B2G_API int b2g_workspace_reset(void* workspace, size_t bytes, void* stream);
+
+/* a16w16: C = A * B^T, A/B fp16 or bf16 (`in_dtype`), C fp16 or bf16
+ * (`out_dtype`). lda, ldb and ldc must be multiples of 8 elements (16-byte
+ * rows); K itself is free. */
+B2G_API int b2g_gemm_f16(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
+                 int M, int N, int K, int in_dtype, int out_dtype, void* workspace,
+                 size_t workspace_bytes, int* status, void* stream);
+
+/* a8w8: C = A * B^T with A/B e5m2 bytes. With sfa == sfb == NULL the product
+ * is unscaled (the reference's a8w8 contract, usually out_dtype = fp16).
+ * Otherwise both scale tensors are E8M0 bytes of logical shape (rows, K/32)
+ * with element strides (s0, s1) - any order, e.g. the reference's
+ * M-contiguous (1, rows_pad) - and K must be a multiple of 32. */
+B2G_API int b2g_gemm_f8(const void* A, int64_t lda, const void* B, int64_t ldb, const uint8_t* sfa,
+                int64_t sfa_s0, int64_t sfa_s1, const uint8_t* sfb, int64_t sfb_s0,
+                int64_t sfb_s1, void* C, int64_t ldc, int M, int N, int K, int out_dtype,
+                void* workspace, size_t workspace_bytes, int* status, void* stream);
+
+/* a4w4: C = dequant(A) * dequant(B)^T with A (M, K/2) and B (N, K/2) packed
+ * e2m1 bytes (low nibble = even k), lda/ldb in bytes, E8M0 scales as in
+ * b2g_gemm_f8. K is the logical (unpacked) depth, a multiple of 32. */
+B2G_API int b2g_gemm_mxf4(const uint8_t* A, int64_t lda, const uint8_t* B, int64_t ldb,
+                  const uint8_t* sfa, int64_t sfa_s0, int64_t sfa_s1, const uint8_t* sfb,
+                  int64_t sfb_s0, int64_t sfb_s1, void* C, int64_t ldc, int M, int N, int K,
+                  int out_dtype, void* workspace, size_t workspace_bytes, int* status,
+                  void* stream);
+
+/* Quantise fp32 `src` (rows x K, row stride ld) to MXFP4: per row and 32-K
+ * block, scale exponent s = floor(log2(max|x|)) - 2 (E8M0 byte s + 127,
+ * clamped to [0, 254]; an all-zero block gets byte 0; a block with a NaN or
+ * an infinity gets byte 255 and zero codes), codes = E2M1 round-to-nearest-even
+ * with saturation to +-6 of x * 2^-s, two per byte with the even k in the low
+ * nibble. q is rows x K/2 bytes (row stride ldq); scales go to
+ * scales[r * sc_s0 + j * sc_s1]. K must be a multiple of 32. */
+B2G_API int b2g_quant_mxfp4(const float* src, int64_t ld, int rows, int K, uint8_t* q, int64_t ldq,
+                    uint8_t* scales, int64_t sc_s0, int64_t sc_s1, void* stream);
+
+/* Quantise fp32 `src` to e5m2 with given E8M0 scales: q = e5m2_rne(x * 2^-(e-127))
+ * where e = scales[r * sc_s0 + (k/32) * sc_s1] (non-saturating, the rounding of
+ * torch's float -> float8_e5m2 cast). K must be a multiple of 32. */
+B2G_API int b2g_quant_mxe5m2(const float* src, int64_t ld, int rows, int K, const uint8_t* scales,
+                     int64_t sc_s0, int64_t sc_s1, uint8_t* q, int64_t ldq, void* stream);
+
+/* Elementwise cast of n contiguous values of `src_dtype` (B2G_DT_*) to e5m2,
+ * round-to-nearest-even, non-saturating (torch's Tensor.to(float8_e5m2)). */
+B2G_API int b2g_cast_e5m2(const void* src, int src_dtype, int64_t n, uint8_t* dst, void* stream);
+
+/* ---- process-wide tuning and test options (b2g_set_option keys) ----
+ * They change how later launches are planned; set them before computing a
+ * workspace size and do not change them while GEMMs are in flight. */
+#define B2G_OPT_PAIR 1        /* 1 (default): cta_group::2 CTA pairs for f16/bf16/e5m2 */
+#define B2G_OPT_SK_MODE 2     /* 0: data-parallel only; 1 (default): stream-K over the
+                                 partial last wave; 2: stream-K over the last full
+                                 wave plus the partial one */
+#define B2G_OPT_GROUP_M 3     /* raster group height in tiles (default 8) */
+#define B2G_OPT_MIN_SK_ITERS 4 /* minimum k-iterations per stream-K unit (default 4) */
+#define B2G_OPT_TIMEOUT_MS 5  /* bounded-wait deadline in ms (default 2000) */
+#define B2G_OPT_INJECT_FLAG_TIMEOUT 6 /* test hook: stream-K owners wait for a flag
+                                         value no contributor writes, so the wait
+                                         expires and the status word is set */
+#define B2G_OPT_MAX_UNITS 7   /* cap on persistent work units (0 = one per SM / pair) */
+
+B2G_API int b2g_set_option(int key, int64_t value);
+B2G_API int64_t b2g_get_option(int key);
+
+/* Host-only view of the persistent schedule for a device with `num_sms` SMs
+ * (no GPU needed). out[0..8] = {cta_group, tiles_m, tiles_n, k_iters, units,
+ * dp_tiles, sk_units, launched_units, group_m}. */
+B2G_API int b2g_plan_query(int kind, int M, int N, int K, int num_sms, int32_t* out, int out_len);
+
+/* Work items of one unit in execution order, 8 ints each: {tile, tm, tn,
+ * k_begin, k_end, role (0 full, 1 stream-K owner, 2 contributor),
+ * first_contrib, last_contrib}. Returns the item count (items may be NULL). */
+B2G_API int b2g_plan_items(int kind, int M, int N, int K, int num_sms, int unit, int32_t* items,
+                   int max_items);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B2G_H_ */

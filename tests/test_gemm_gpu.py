@@ -1,0 +1,268 @@
+"""GEMM parity on a B200: the sm_100a kernels (through the C ABI) against the
+CPU oracle on the same seeded inputs, plus the golden vectors the reference's
+own functions produced.
+
+Tolerances: normalised max-abs error max|C - C_ref| / max|C_ref| <= 1e-2 for
+FP16/BF16 and <= 3e-2 for BF8/MXFP4, plus the reference's own
+allclose(atol=0.1, rtol=0) check (kernels/gemm/intra_wave/*/bench.py)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+from conftest import golden
+
+from gfx950_gluon_tutorials_b200 import _lib, a4w4, a8w8, a16w16, ops
+from oracle import mx
+
+pytestmark = pytest.mark.gpu
+
+TOL_F16 = 1e-2
+TOL_F8 = 3e-2
+
+
+def bits16(t: torch.Tensor) -> np.ndarray:
+    return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+def as_f32(t: torch.Tensor) -> np.ndarray:
+    return t.float().cpu().numpy()
+
+
+def assert_close(c: np.ndarray, ref: np.ndarray, tol: float):
+    err = mx.normalised_max_abs(c, ref)
+    assert err <= tol, f"normalised max-abs error {err:.3e} > {tol}"
+    assert np.allclose(c, ref, atol=1e-1, rtol=0), "reference allclose(atol=0.1) failed"
+
+
+@pytest.fixture(params=[
+    dict(pair=1, sk=1, min_sk=4, units=0),
+    dict(pair=0, sk=1, min_sk=4, units=0),
+    dict(pair=1, sk=2, min_sk=1, units=0),
+    dict(pair=0, sk=0, min_sk=4, units=0),
+    dict(pair=1, sk=1, min_sk=1, units=5),   # few units: deep stream-K splits
+    dict(pair=0, sk=2, min_sk=1, units=7),
+], ids=lambda d: f"pair{d['pair']}-sk{d['sk']}-min{d['min_sk']}-u{d['units']}")
+def sched(request, cuda_device):
+    keys = {"pair": _lib.OPT_PAIR, "sk": _lib.OPT_SK_MODE, "min_sk": _lib.OPT_MIN_SK_ITERS,
+            "units": _lib.OPT_MAX_UNITS}
+    old = {k: _lib.get_option(v) for k, v in keys.items()}
+    for k, v in request.param.items():
+        _lib.set_option(keys[k], v)
+    yield request.param
+    for k, v in old.items():
+        _lib.set_option(keys[k], v)
+    ops.check_status(cuda_device)
+
+
+F16_SHAPES = [(128, 256, 64), (256, 512, 512), (300, 700, 200), (1000, 1000, 1024),
+              (64, 2048, 4096), (2048, 96, 136)]
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["fp16", "bf16"])
+@pytest.mark.parametrize("shape", F16_SHAPES, ids=lambda s: "x".join(map(str, s)))
+def test_a16w16_matches_oracle(sched, dtype, shape):
+    M, N, K = shape
+    g = torch.Generator(device="cuda").manual_seed(M * 7 + N * 3 + K)
+    a = torch.rand((M, K), generator=g, device="cuda", dtype=torch.float32).to(dtype) - 0.5
+    b_t = torch.rand((N, K), generator=g, device="cuda", dtype=torch.float32).to(dtype) - 0.5
+    c = ops.gemm_f16(a, b_t)
+    ops.check_status()
+    if dtype == torch.float16:
+        ref = mx.gemm_f16_ref(a.cpu().numpy(), b_t.cpu().numpy(), "f16").astype(np.float32)
+    else:
+        ref = mx.bf16_bits_to_f32(mx.gemm_f16_ref(bits16(a), bits16(b_t), "bf16"))
+    assert_close(as_f32(c), ref, TOL_F16)
+
+
+@pytest.mark.parametrize("name,dtype", [("a16w16_f16_128x256x320.npz", torch.float16),
+                                        ("a16w16_bf16_128x256x320.npz", torch.bfloat16)])
+def test_a16w16_golden_via_reference_api(cuda_device, name, dtype):
+    g = golden(name)
+    if dtype == torch.float16:
+        a = torch.from_numpy(g["a"]).cuda()
+        b_t = torch.from_numpy(g["b_t"]).cuda()
+        ref = g["c"].astype(np.float32)
+    else:
+        a = torch.from_numpy(g["a"].view(np.int16)).view(torch.bfloat16).cuda()
+        b_t = torch.from_numpy(g["b_t"].view(np.int16)).view(torch.bfloat16).cuda()
+        ref = mx.bf16_bits_to_f32(g["c"])
+    c = a16w16.matmul(a, b_t.T)  # the reference bench passes b as a (K, N) view
+    ops.check_status()
+    assert c.dtype == dtype
+    assert_close(as_f32(c), ref, TOL_F16)
+
+
+def test_a16w16_explicit_c_and_strided_rows(cuda_device):
+    M, N, K = 192, 320, 256
+    a_store = torch.randn((M, K + 64), device="cuda", dtype=torch.float16)
+    a = a_store[:, :K]                       # row stride K + 64
+    b_t = torch.randn((N, K), device="cuda", dtype=torch.float16)
+    c_store = torch.full((M, N + 8), float("nan"), device="cuda", dtype=torch.float16)
+    c = c_store[:, :N]
+    a16w16.matmul_kernel_only(a, b_t, c)
+    ops.check_status()
+    ref = mx.gemm_f16_ref(a.cpu().numpy(), b_t.cpu().numpy()).astype(np.float32)
+    assert_close(as_f32(c), ref, TOL_F16)
+    assert torch.isnan(c_store[:, N:]).all(), "wrote outside C"
+
+
+def test_a16w16_full_size_sampled_rows(cuda_device):
+    """Config-1 size (4096 x 4096 x 8192): the whole C against the oracle on a
+    seeded sample of 256 rows, and against the exact GPU product for all rows."""
+    M = N = 4096
+    K = 8192
+    g = torch.Generator(device="cuda").manual_seed(1)
+    a = (torch.randn((M, K), generator=g, device="cuda") / K ** 0.5).half()
+    b_t = (torch.randn((N, K), generator=g, device="cuda") / K ** 0.5).half()
+    c = ops.gemm_f16(a, b_t)
+    ops.check_status()
+    rows = torch.randperm(M, generator=torch.Generator().manual_seed(2))[:256]
+    ref = mx.gemm_f16_ref(a[rows.cuda()].cpu().numpy(), b_t.cpu().numpy()).astype(np.float32)
+    assert_close(as_f32(c[rows.cuda()]), ref, TOL_F16)
+    full = (a.float() @ b_t.float().T)
+    err = ((c.float() - full).abs().max() / full.abs().max()).item()
+    assert err <= TOL_F16
+
+
+E5M2_SHAPES = [(128, 256, 128), (256, 512, 1024), (300, 700, 208), (1000, 1000, 2048)]
+
+
+@pytest.mark.parametrize("shape", E5M2_SHAPES, ids=lambda s: "x".join(map(str, s)))
+def test_a8w8_unscaled_matches_oracle(sched, shape):
+    M, N, K = shape
+    g = torch.Generator(device="cuda").manual_seed(M + N + K)
+    a = (torch.rand((M, K), generator=g, device="cuda").half() - 0.5).to(torch.float8_e5m2)
+    b = (torch.rand((N, K), generator=g, device="cuda").half().T - 0.5).to(torch.float8_e5m2)
+    c = a8w8.matmul(a, b)
+    ops.check_status()
+    assert c.dtype == torch.float16
+    ref = mx.gemm_e5m2_ref(a.view(torch.uint8).cpu().numpy(),
+                           b.T.contiguous().view(torch.uint8).cpu().numpy()).astype(np.float32)
+    assert_close(as_f32(c), ref, TOL_F8)
+
+
+def test_a8w8_golden(cuda_device):
+    g = golden("a8w8_e5m2_128x256x512.npz")
+    a = torch.from_numpy(g["a"]).cuda().view(torch.float8_e5m2)
+    b_t = torch.from_numpy(g["b_t"]).cuda().view(torch.float8_e5m2)
+    c = a8w8.matmul(a, b_t.T)
+    ops.check_status()
+    assert_close(as_f32(c), g["c"].astype(np.float32), TOL_F8)
+
+
+def _mx_e5m2_inputs(M, N, K, seed):
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    xa = torch.randn((M, K), generator=gen, device="cuda")
+    xb = torch.randn((N, K), generator=gen, device="cuda")
+    ea = torch.randint(125, 130, (M, K // 32), generator=gen, device="cuda").to(torch.uint8)
+    eb = torch.randint(125, 130, (N, K // 32), generator=gen, device="cuda").to(torch.uint8)
+    return xa, xb, ea, eb
+
+
+@pytest.mark.parametrize("shape", [(128, 256, 128), (256, 512, 1024), (200, 300, 96),
+                                   (1024, 768, 2048)], ids=lambda s: "x".join(map(str, s)))
+def test_a8w8_scaled_matches_oracle(sched, shape):
+    M, N, K = shape
+    xa, xb, ea, eb = _mx_e5m2_inputs(M, N, K, M * N + K)
+    qa = ops.quantize_mxe5m2(xa, ea)
+    qb = ops.quantize_mxe5m2(xb, eb)
+    # the reference-style M-contiguous storage for A's scales
+    ea_mc = ea.T.contiguous().T
+    c = a8w8.matmul_scaled(qa, qb.T, ea_mc, eb)
+    ops.check_status()
+    ref = mx.bf16_bits_to_f32(mx.gemm_mxe5m2_ref(
+        qa.view(torch.uint8).cpu().numpy(), qb.view(torch.uint8).cpu().numpy(),
+        ea.cpu().numpy(), eb.cpu().numpy()))
+    assert_close(as_f32(c), ref, TOL_F8)
+
+
+def _reference_style_mxfp4(M, N, K, seed):
+    """Same recipe as the reference generator (kernels/gemm/intra_wave/a4w4/bench.py:115-146):
+    random nibbles, scale bytes 124..127, A scales M-contiguous with M_pad rows."""
+    g = torch.Generator().manual_seed(seed)
+    a = (torch.randint(0, 16, (M, K // 2), generator=g, dtype=torch.uint8) << 4) | \
+        torch.randint(0, 16, (M, K // 2), generator=g, dtype=torch.uint8)
+    b = (torch.randint(0, 16, (N, K // 2), generator=g, dtype=torch.uint8) << 4) | \
+        torch.randint(0, 16, (N, K // 2), generator=g, dtype=torch.uint8)
+    m_pad = (M + 255) // 256 * 256
+    sa = torch.randint(124, 128, (K // 32, m_pad), generator=g, dtype=torch.uint8).cuda().T[:M]
+    sb = torch.randint(124, 128, (K // 32, N), generator=g, dtype=torch.uint8).cuda().T
+    return a.cuda(), b.cuda(), sa, sb
+
+
+@pytest.mark.parametrize("shape", [(128, 256, 256), (256, 512, 1024), (200, 320, 1024),
+                                   (1000, 600, 2048), (128, 256, 64)],
+                         ids=lambda s: "x".join(map(str, s)))
+def test_a4w4_reference_style_matches_oracle(sched, shape):
+    M, N, K = shape
+    a, b, sa, sb = _reference_style_mxfp4(M, N, K, M + 3 * N + K)
+    c = a4w4.matmul(a, b, sa, sb)
+    ops.check_status()
+    ref_bits = mx.gemm_mxfp4_ref(a.cpu().numpy(), b.cpu().numpy(), sa.cpu().numpy(),
+                                 sb.cpu().numpy())
+    got_bits = bits16(c)
+    assert_close(mx.bf16_bits_to_f32(got_bits), mx.bf16_bits_to_f32(ref_bits), TOL_F8)
+    exact = float(np.mean(got_bits == ref_bits))
+    print(f"mxfp4 {M}x{N}x{K}: bit-exact fraction {exact:.6f}")
+
+
+@pytest.mark.parametrize("name", ["mxfp4_ref_128x256x256.npz", "mxfp4_ref_256x256x512.npz",
+                                  "mxfp4_ref_200x320x1024.npz"])
+def test_a4w4_golden(cuda_device, name):
+    g = golden(name)
+    a = torch.from_numpy(g["a"]).cuda()
+    b = torch.from_numpy(g["b"]).cuda()
+    sa = torch.from_numpy(g["a_scales"]).cuda()
+    sb = torch.from_numpy(g["b_scales"]).cuda()
+    c = a4w4.matmul(a, b, sa, sb)
+    ops.check_status()
+    got = bits16(c)
+    assert_close(mx.bf16_bits_to_f32(got), mx.bf16_bits_to_f32(g["c_bf16"]), TOL_F8)
+
+
+@pytest.mark.parametrize("shape", [(256, 256, 512), (512, 1024, 4096)],
+                         ids=lambda s: "x".join(map(str, s)))
+def test_a4w4_quantised_normal_inputs(sched, shape):
+    """Config-3 recipe: N(0,1) data through the GPU quantiser, then the GEMM."""
+    M, N, K = shape
+    gen = torch.Generator(device="cuda").manual_seed(11)
+    xa = torch.randn((M, K), generator=gen, device="cuda")
+    xb = torch.randn((N, K), generator=gen, device="cuda")
+    qa, sa = ops.quantize_mxfp4(xa)
+    qb, sb = ops.quantize_mxfp4(xb)
+    c = a4w4.matmul(qa, qb, sa, sb)
+    ops.check_status()
+    ref = mx.gemm_mxfp4_ref(qa.cpu().numpy(), qb.cpu().numpy(), sa.cpu().numpy(),
+                            sb.cpu().numpy())
+    assert_close(as_f32(c), mx.bf16_bits_to_f32(ref), TOL_F8)
+
+
+def test_a4w4_full_size_sampled_rows(cuda_device):
+    M = N = 4096
+    K = 8192
+    gen = torch.Generator(device="cuda").manual_seed(3)
+    qa, sa = ops.quantize_mxfp4(torch.randn((M, K), generator=gen, device="cuda"))
+    qb, sb = ops.quantize_mxfp4(torch.randn((N, K), generator=gen, device="cuda"))
+    c = a4w4.matmul(qa, qb, sa, sb)
+    ops.check_status()
+    rows = torch.randperm(M, generator=torch.Generator().manual_seed(4))[:128].cuda()
+    ref = mx.gemm_mxfp4_ref(qa[rows].cpu().numpy(), qb.cpu().numpy(),
+                            sa[rows].cpu().numpy(), sb.cpu().numpy())
+    assert_close(as_f32(c[rows]), mx.bf16_bits_to_f32(ref), TOL_F8)
+
+
+def test_repeated_calls_are_deterministic(cuda_device):
+    """Stream-K reduces partials in a fixed order: identical inputs, identical bits."""
+    old = _lib.get_option(_lib.OPT_MIN_SK_ITERS)
+    _lib.set_option(_lib.OPT_MIN_SK_ITERS, 1)
+    try:
+        a = torch.randn((512, 4096), device="cuda", dtype=torch.bfloat16)
+        b_t = torch.randn((512, 4096), device="cuda", dtype=torch.bfloat16)
+        c0 = ops.gemm_f16(a, b_t)
+        for _ in range(3):
+            assert torch.equal(ops.gemm_f16(a, b_t), c0)
+        ops.check_status()
+    finally:
+        _lib.set_option(_lib.OPT_MIN_SK_ITERS, old)

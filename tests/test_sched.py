@@ -1,0 +1,90 @@
+"""Host-side checks of the persistent DP + stream-K schedule (no GPU).
+
+The kernel walks exactly these work lists, so proving coverage here proves the
+device does every k-iteration of every tile exactly once."""
+
+from __future__ import annotations
+
+from collections import defaultdict
+
+import pytest
+
+from gfx950_gluon_tutorials_b200 import _lib, ops
+
+ROLE_FULL, ROLE_OWNER, ROLE_CONTRIB = 0, 1, 2
+
+SHAPES = [
+    (_lib.KIND_F16, 4096, 4096, 8192),     # 256 pair tiles over 74 pairs
+    (_lib.KIND_F16, 3840, 3840, 8192),     # 225 tiles
+    (_lib.KIND_BF16, 512, 512, 1024),      # fewer tiles than units: all stream-K
+    (_lib.KIND_F16, 300, 700, 200),        # ragged everything
+    (_lib.KIND_E5M2, 4096, 4096, 8192),
+    (_lib.KIND_MXE5M2, 4096, 4096, 8192),
+    (_lib.KIND_MXFP4, 4096, 4096, 8192),
+    (_lib.KIND_MXFP4, 16384, 6656, 16384),  # one 8-GPU shard of the large config
+    (_lib.KIND_MXFP4, 128, 256, 64),       # a single tile, single k-iteration
+]
+
+
+@pytest.fixture(params=[(0, 1), (1, 1), (2, 1), (1, 0), (2, 0)],
+                ids=lambda p: f"sk{p[0]}-pair{p[1]}")
+def options(request):
+    sk, pair = request.param
+    old = {k: _lib.get_option(k) for k in (_lib.OPT_SK_MODE, _lib.OPT_PAIR,
+                                           _lib.OPT_MIN_SK_ITERS)}
+    _lib.set_option(_lib.OPT_SK_MODE, sk)
+    _lib.set_option(_lib.OPT_PAIR, pair)
+    _lib.set_option(_lib.OPT_MIN_SK_ITERS, 1)
+    yield
+    for k, v in old.items():
+        _lib.set_option(k, v)
+
+
+@pytest.mark.parametrize("num_sms", [148, 132, 20])
+@pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "x".join(map(str, s)))
+def test_schedule_covers_every_iteration_once(options, shape, num_sms):
+    kind, M, N, K = shape
+    p = ops.plan(kind, M, N, K, num_sms)
+    tiles = p["tiles_m"] * p["tiles_n"]
+    cover = defaultdict(int)
+    owners = {}
+    contrib_of = defaultdict(list)
+    coords = {}
+    for u in range(p["launched"]):
+        items = ops.plan_items(kind, M, N, K, u, num_sms)
+        seen_sk = False
+        for idx, (t, tm, tn, kb, ke, role, first, last) in enumerate(items):
+            assert 0 <= t < tiles and 0 <= tm < p["tiles_m"] and 0 <= tn < p["tiles_n"]
+            assert coords.setdefault(t, (tm, tn)) == (tm, tn)
+            assert 0 <= kb < ke <= p["k_iters"]
+            for k in range(kb, ke):
+                cover[(t, k)] += 1
+            if role == ROLE_CONTRIB:
+                # a unit contributes at most once, in its first stream-K segment
+                assert not seen_sk
+                assert u < p["sk_units"]
+                contrib_of[t].append(u)
+            if role == ROLE_OWNER:
+                assert kb == 0 and ke < p["k_iters"]
+                assert t not in owners
+                owners[t] = (u, first, last)
+                assert idx == len(items) - 1  # the owner's wait is its last item
+            if t >= p["dp_tiles"]:
+                seen_sk = True
+    assert len(cover) == tiles * p["k_iters"]
+    assert all(v == 1 for v in cover.values())
+    assert len(set(coords.values())) == tiles
+    for t, units in contrib_of.items():
+        u, first, last = owners[t]
+        assert units == list(range(first, last + 1))
+        assert u < first
+    assert set(owners) == set(contrib_of)
+
+
+def test_default_plan_for_the_headline_config():
+    p = ops.plan(_lib.KIND_F16, 4096, 4096, 8192, 148)
+    assert p["cta_group"] == 2 and p["units"] == 74
+    assert p["tiles_m"] * p["tiles_n"] == 256
+    assert p["dp_tiles"] == 222 and p["sk_units"] == 74
+    p = ops.plan(_lib.KIND_MXFP4, 4096, 4096, 8192, 148)
+    assert p["cta_group"] == 1 and p["units"] == 148 and p["k_iters"] == 32
