@@ -142,7 +142,8 @@ def quantize_mxfp4(x: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
     scales[nonfinite] = 255
     scales[zero] = 0
     mul = _exp2i(-s)
-    y = blk * mul[:, :, None]
+    with np.errstate(over="ignore", invalid="ignore"):  # non-finite blocks are zeroed below
+        y = blk * mul[:, :, None]
     codes = e2m1_code(y)
     codes[nonfinite] = 0
     codes = codes.reshape(rows, K)
@@ -157,7 +158,8 @@ def quantize_mxe5m2(x: np.ndarray, scales: np.ndarray) -> np.ndarray:
     rows, K = x.shape
     e = np.asarray(scales, dtype=np.int64)
     mul = _exp2i(127 - e)
-    y = x.reshape(rows, K // 32, 32) * mul[:, :, None]
+    with np.errstate(over="ignore", invalid="ignore"):  # overflow -> inf, as on the GPU
+        y = x.reshape(rows, K // 32, 32) * mul[:, :, None]
     q = f32_to_e5m2(y)
     q[e == 255] = 0
     return q.reshape(rows, K)

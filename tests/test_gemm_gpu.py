@@ -30,10 +30,15 @@ def as_f32(t: torch.Tensor) -> np.ndarray:
     return t.float().cpu().numpy()
 
 
-def assert_close(c: np.ndarray, ref: np.ndarray, tol: float):
+def assert_close(c: np.ndarray, ref: np.ndarray, tol: float, ref_atol: bool = True):
+    """Normalised max-abs error within `tol`; with `ref_atol`, also the reference's
+    allclose(atol=0.1, rtol=0). That absolute check only means something for the
+    reference's own input recipes (rand - 0.5, random nibbles), whose outputs are
+    small; N(0,1)-scaled operands give outputs near 100 where one bf16 ulp is 0.5."""
     err = mx.normalised_max_abs(c, ref)
     assert err <= tol, f"normalised max-abs error {err:.3e} > {tol}"
-    assert np.allclose(c, ref, atol=1e-1, rtol=0), "reference allclose(atol=0.1) failed"
+    if ref_atol:
+        assert np.allclose(c, ref, atol=1e-1, rtol=0), "reference allclose(atol=0.1) failed"
 
 
 @pytest.fixture(params=[
@@ -104,7 +109,7 @@ def test_a16w16_explicit_c_and_strided_rows(cuda_device):
     a16w16.matmul_kernel_only(a, b_t, c)
     ops.check_status()
     ref = mx.gemm_f16_ref(a.cpu().numpy(), b_t.cpu().numpy()).astype(np.float32)
-    assert_close(as_f32(c), ref, TOL_F16)
+    assert_close(as_f32(c), ref, TOL_F16, ref_atol=False)
     assert torch.isnan(c_store[:, N:]).all(), "wrote outside C"
 
 
@@ -175,7 +180,7 @@ def test_a8w8_scaled_matches_oracle(sched, shape):
     ref = mx.bf16_bits_to_f32(mx.gemm_mxe5m2_ref(
         qa.view(torch.uint8).cpu().numpy(), qb.view(torch.uint8).cpu().numpy(),
         ea.cpu().numpy(), eb.cpu().numpy()))
-    assert_close(as_f32(c), ref, TOL_F8)
+    assert_close(as_f32(c), ref, TOL_F8, ref_atol=False)
 
 
 def _reference_style_mxfp4(M, N, K, seed):
@@ -236,7 +241,7 @@ def test_a4w4_quantised_normal_inputs(sched, shape):
     ops.check_status()
     ref = mx.gemm_mxfp4_ref(qa.cpu().numpy(), qb.cpu().numpy(), sa.cpu().numpy(),
                             sb.cpu().numpy())
-    assert_close(as_f32(c), mx.bf16_bits_to_f32(ref), TOL_F8)
+    assert_close(as_f32(c), mx.bf16_bits_to_f32(ref), TOL_F8, ref_atol=False)
 
 
 def test_a4w4_full_size_sampled_rows(cuda_device):
@@ -250,7 +255,7 @@ def test_a4w4_full_size_sampled_rows(cuda_device):
     rows = torch.randperm(M, generator=torch.Generator().manual_seed(4))[:128].cuda()
     ref = mx.gemm_mxfp4_ref(qa[rows].cpu().numpy(), qb.cpu().numpy(),
                             sa[rows].cpu().numpy(), sb.cpu().numpy())
-    assert_close(as_f32(c[rows]), mx.bf16_bits_to_f32(ref), TOL_F8)
+    assert_close(as_f32(c[rows]), mx.bf16_bits_to_f32(ref), TOL_F8, ref_atol=False)
 
 
 def test_repeated_calls_are_deterministic(cuda_device):
