@@ -21,13 +21,14 @@ namespace {
 
 // ------------------------------------------------------------- options --
 struct Options {
-  std::atomic<int64_t> pair_f16{1};      // cta_group::2 for f16/bf16/e5m2
-  std::atomic<int64_t> sk_mode{1};       // see make_plan
-  std::atomic<int64_t> group_m{8};
+  std::atomic<int64_t> pair{1};          // cta_group::2 CTA pairs
+  std::atomic<int64_t> sk_mode{3};       // see make_plan
+  std::atomic<int64_t> group_m{1};
   std::atomic<int64_t> min_sk_iters{4};
   std::atomic<int64_t> timeout_ms{2000};
   std::atomic<int64_t> inject{0};
   std::atomic<int64_t> max_units{0};     // 0 = one unit per SM (pair)
+  std::atomic<int64_t> prefetch{0};      // k-iterations pulled into L2 ahead of the ring
 };
 Options g_opt;
 
@@ -69,7 +70,7 @@ int pair_capacity(int dev, int sms) {
                            static_cast<int>(SP::kDynBytes)) == cudaSuccess) {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(static_cast<unsigned>(sms & ~1), 1, 1);
-    cfg.blockDim = dim3(192, 1, 1);
+    cfg.blockDim = dim3(SP::kThreads, 1, 1);
     cfg.dynamicSmemBytes = SP::kDynBytes;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -119,16 +120,19 @@ struct Geometry {
   int cg;
   SkPlan plan;
   int launched;
-  int sf_groups;
-  int sfa_row_blocks, sfb_row_blocks;
+  int sf_groups;  // 4-scale groups per row of the blocked scale layout
   size_t flags_off, flags_bytes, partial_off, partial_bytes;
   size_t sfa_off, sfa_bytes, sfb_off, sfb_bytes, total;
 };
 
+int64_t blocked_scale_bytes(int64_t rows, int64_t K) {
+  return ((rows + 127) / 128) * ((K / 32 + 3) / 4) * 512;
+}
+
 // `pair_cap`: how many CTA pairs the device can hold at once (0 = sms / 2).
 Geometry geometry(int kind, int M, int N, int K, int sms, int pair_cap = 0) {
   Geometry g{};
-  g.cg = (!is_scaled(kind) && g_opt.pair_f16.load() != 0) ? 2 : 1;
+  g.cg = g_opt.pair.load() != 0 ? 2 : 1;
   int units = g.cg == 2 ? sms / 2 : sms;
   if (g.cg == 2 && pair_cap > 0 && pair_cap < units) units = pair_cap;
   const int64_t mu = g_opt.max_units.load();
@@ -142,22 +146,24 @@ Geometry geometry(int kind, int M, int N, int K, int sms, int pair_cap = 0) {
                      static_cast<int>(g_opt.min_sk_iters.load()));
   g.launched = std::min(units, std::max(g.plan.dp_tiles, g.plan.sk_units));
   if (g.launched < 1) g.launched = 1;
-  const int gps = kind == B2G_KIND_MXFP4 ? 2 : 1;
-  g.sf_groups = is_scaled(kind) ? k_iters * gps : 0;
-  g.sfa_row_blocks = is_scaled(kind) ? tiles_m * g.cg : 0;
-  g.sfb_row_blocks = is_scaled(kind) ? tiles_n * 2 : 0;
+  // The flag region has one fixed size per device (every unit of every plan
+  // fits: units * cta_group <= SMs), so partial sums written by one call can
+  // never sit where a later call with another geometry looks for its flags.
   size_t off = 0;
   g.flags_off = off;
-  g.flags_bytes = align256(static_cast<size_t>(g.plan.sk_units) * g.cg * 4 * sizeof(uint32_t));
+  g.flags_bytes = g.plan.sk_units > 0 ? align256(static_cast<size_t>(sms) * 4 * sizeof(uint32_t))
+                                      : 0;
   off += g.flags_bytes;
   g.partial_off = off;
   g.partial_bytes = static_cast<size_t>(g.plan.sk_units) * g.cg * 128 * 256 * sizeof(float);
   off += align256(g.partial_bytes);
+  // scale relayout targets (scaled kinds, unless the caller passes blocked scales)
+  g.sf_groups = is_scaled(kind) ? (K / 32 + 3) / 4 : 0;
   g.sfa_off = off;
-  g.sfa_bytes = static_cast<size_t>(g.sfa_row_blocks) * g.sf_groups * 512;
+  g.sfa_bytes = is_scaled(kind) ? static_cast<size_t>(blocked_scale_bytes(M, K)) : 0;
   off += align256(g.sfa_bytes);
   g.sfb_off = off;
-  g.sfb_bytes = static_cast<size_t>(g.sfb_row_blocks) * g.sf_groups * 512;
+  g.sfb_bytes = is_scaled(kind) ? static_cast<size_t>(blocked_scale_bytes(N, K)) : 0;
   off += align256(g.sfb_bytes);
   g.total = off;
   return g;
@@ -180,7 +186,8 @@ int encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t
 
 template <int KIND, int CG, bool OB>
 int launch_gemm_t(const GemmParams& prm, int units, cudaStream_t stream) {
-  constexpr int kStages = CG == 1 ? 4 : 6;
+  constexpr bool kScaled = KindTraits<KIND>::kScaled;
+  constexpr int kStages = CG == 1 ? 4 : (kScaled ? 5 : 6);
   using SP = SmemPlan<KIND, CG, kStages>;
   static_assert(SP::kDynBytes <= 232448, "shared memory plan exceeds 227 KB");
   auto kern = gemm_kernel<KIND, CG, kStages, OB>;
@@ -196,7 +203,7 @@ int launch_gemm_t(const GemmParams& prm, int units, cudaStream_t stream) {
   }
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(static_cast<unsigned>(units * CG), 1, 1);
-  cfg.blockDim = dim3(192, 1, 1);
+  cfg.blockDim = dim3(SP::kThreads, 1, 1);
   cfg.dynamicSmemBytes = SP::kDynBytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -230,8 +237,12 @@ int dispatch(int kind, int cg, const GemmParams& prm, int units, int out_dtype,
     case B2G_KIND_E5M2:
       return cg == 2 ? launch_gemm_out<kKindE5M2, 2>(prm, units, out_dtype, s)
                      : launch_gemm_out<kKindE5M2, 1>(prm, units, out_dtype, s);
-    case B2G_KIND_MXE5M2: return launch_gemm_out<kKindMXE5M2, 1>(prm, units, out_dtype, s);
-    case B2G_KIND_MXFP4: return launch_gemm_out<kKindMXFP4, 1>(prm, units, out_dtype, s);
+    case B2G_KIND_MXE5M2:
+      return cg == 2 ? launch_gemm_out<kKindMXE5M2, 2>(prm, units, out_dtype, s)
+                     : launch_gemm_out<kKindMXE5M2, 1>(prm, units, out_dtype, s);
+    case B2G_KIND_MXFP4:
+      return cg == 2 ? launch_gemm_out<kKindMXFP4, 2>(prm, units, out_dtype, s)
+                     : launch_gemm_out<kKindMXFP4, 1>(prm, units, out_dtype, s);
     default: return B2G_EINVAL;
   }
 }
@@ -279,6 +290,8 @@ int check_call(const GemmCall& c) {
   if (c.lda * eb < rb || c.ldb * eb < rb || c.ldc < c.N) return B2G_ESTRIDE;
   if (is_scaled(c.kind) && (c.sfa_s0 < 0 || c.sfa_s1 < 0 || c.sfb_s0 < 0 || c.sfb_s1 < 0))
     return B2G_ESTRIDE;
+  if (is_scaled(c.kind) && ((c.sfa_s0 == 0) != (c.sfa_s1 == 0) || (c.sfb_s0 == 0) != (c.sfb_s1 == 0)))
+    return B2G_ESTRIDE;
   return B2G_OK;
 }
 
@@ -309,18 +322,31 @@ int run_gemm(const GemmCall& c) {
                  static_cast<uint64_t>(c.M), static_cast<uint64_t>(c.ldc * 2), 32, 32,
                  CU_TENSOR_MAP_SWIZZLE_64B);
   if (rc != B2G_OK) return rc;
-
   if (is_scaled(c.kind)) {
-    uint8_t* sfa_blk = ws + g.sfa_off;
-    uint8_t* sfb_blk = ws + g.sfb_off;
-    cudaError_t e = launch_sf_relayout(c.sfa, c.sfa_s0, c.sfa_s1, c.M, c.K / 32,
-                                       g.sfa_row_blocks, g.sf_groups, sfa_blk, c.stream);
-    if (e != cudaSuccess) return static_cast<int>(e);
-    e = launch_sf_relayout(c.sfb, c.sfb_s0, c.sfb_s1, c.N, c.K / 32, g.sfb_row_blocks,
-                           g.sf_groups, sfb_blk, c.stream);
-    if (e != cudaSuccess) return static_cast<int>(e);
-    prm.sfa = sfa_blk;
-    prm.sfb = sfb_blk;
+    // scales in the caller's (rows, K/32) layout are relaid into the workspace
+    // in one launch; strides (0, 0) mean the tensor is already blocked
+    const bool a_blocked = c.sfa_s0 == 0 && c.sfa_s1 == 0;
+    const bool b_blocked = c.sfb_s0 == 0 && c.sfb_s1 == 0;
+    const uint8_t* sfa = a_blocked ? c.sfa : ws + g.sfa_off;
+    const uint8_t* sfb = b_blocked ? c.sfb : ws + g.sfb_off;
+    if (!aligned16(sfa) || !aligned16(sfb)) return B2G_EALIGN;
+    if (!a_blocked || !b_blocked) {
+      const cudaError_t e = launch_sf_relayout(
+          a_blocked ? nullptr : c.sfa, c.sfa_s0, c.sfa_s1, c.M, ws + g.sfa_off,
+          b_blocked ? nullptr : c.sfb, c.sfb_s0, c.sfb_s1, c.N, ws + g.sfb_off, c.K / 32,
+          c.stream);
+      if (e != cudaSuccess) return static_cast<int>(e);
+    }
+    const uint32_t gwords = static_cast<uint32_t>(c.kind == B2G_KIND_MXFP4 ? 256 : 128);
+    const uint64_t row_words = static_cast<uint64_t>(g.sf_groups) * 128;
+    rc = encode_2d(&prm.tmSFA, CU_TENSOR_MAP_DATA_TYPE_UINT32, sfa, row_words,
+                   static_cast<uint64_t>((c.M + 127) / 128), row_words * 4, gwords, 1,
+                   CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc != B2G_OK) return rc;
+    rc = encode_2d(&prm.tmSFB, CU_TENSOR_MAP_DATA_TYPE_UINT32, sfb, row_words,
+                   static_cast<uint64_t>((c.N + 127) / 128), row_words * 4, gwords, 2,
+                   CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc != B2G_OK) return rc;
   }
   prm.partials = g.partial_bytes ? reinterpret_cast<float*>(ws + g.partial_off) : nullptr;
   prm.flags = g.flags_bytes ? reinterpret_cast<uint32_t*>(ws + g.flags_off) : nullptr;
@@ -329,8 +355,8 @@ int run_gemm(const GemmCall& c) {
   prm.M = c.M;
   prm.N = c.N;
   prm.K = c.K;
-  prm.sf_groups = g.sf_groups;
   prm.inject = static_cast<int32_t>(g_opt.inject.load());
+  prm.prefetch = static_cast<int32_t>(g_opt.prefetch.load());
   prm.timeout_ns = static_cast<uint64_t>(g_opt.timeout_ms.load()) * 1000000ull;
   return dispatch(c.kind, g.cg, prm, g.launched, c.out_dtype, c.stream);
 }
@@ -466,11 +492,27 @@ int b2g_cast_e5m2(const void* src, int src_dtype, int64_t n, uint8_t* dst, void*
   return e == cudaSuccess ? B2G_OK : static_cast<int>(e);
 }
 
+size_t b2g_scales_blocked_bytes(int rows, int K) {
+  if (rows < 1 || K < 32 || K % 32 != 0) return 0;
+  return static_cast<size_t>(blocked_scale_bytes(rows, K));
+}
+
+int b2g_scales_to_blocked(const uint8_t* src, int64_t s0, int64_t s1, int rows, int K,
+                          uint8_t* dst, void* stream) {
+  if (src == nullptr || dst == nullptr) return B2G_EINVAL;
+  if (rows < 1 || K < 32 || K % 32 != 0) return B2G_ESHAPE;
+  if (s0 < 0 || s1 < 0 || (s0 == 0 && s1 == 0)) return B2G_ESTRIDE;
+  if (!aligned16(dst)) return B2G_EALIGN;
+  const cudaError_t e = launch_sf_relayout(src, s0, s1, rows, dst, nullptr, 0, 0, 0, nullptr,
+                                           K / 32, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? B2G_OK : static_cast<int>(e);
+}
+
 int b2g_set_option(int key, int64_t value) {
   switch (key) {
-    case B2G_OPT_PAIR: g_opt.pair_f16.store(value != 0); return B2G_OK;
+    case B2G_OPT_PAIR: g_opt.pair.store(value != 0); return B2G_OK;
     case B2G_OPT_SK_MODE:
-      if (value < 0 || value > 2) return B2G_EINVAL;
+      if (value < 0 || value > 3) return B2G_EINVAL;
       g_opt.sk_mode.store(value);
       return B2G_OK;
     case B2G_OPT_GROUP_M:
@@ -490,25 +532,30 @@ int b2g_set_option(int key, int64_t value) {
       if (value < 0) return B2G_EINVAL;
       g_opt.max_units.store(value);
       return B2G_OK;
+    case B2G_OPT_L2_PREFETCH:
+      if (value < 0 || value > 64) return B2G_EINVAL;
+      g_opt.prefetch.store(value);
+      return B2G_OK;
     default: return B2G_EINVAL;
   }
 }
 
 int64_t b2g_get_option(int key) {
   switch (key) {
-    case B2G_OPT_PAIR: return g_opt.pair_f16.load();
+    case B2G_OPT_PAIR: return g_opt.pair.load();
     case B2G_OPT_SK_MODE: return g_opt.sk_mode.load();
     case B2G_OPT_GROUP_M: return g_opt.group_m.load();
     case B2G_OPT_MIN_SK_ITERS: return g_opt.min_sk_iters.load();
     case B2G_OPT_TIMEOUT_MS: return g_opt.timeout_ms.load();
     case B2G_OPT_INJECT_FLAG_TIMEOUT: return g_opt.inject.load();
     case B2G_OPT_MAX_UNITS: return g_opt.max_units.load();
+    case B2G_OPT_L2_PREFETCH: return g_opt.prefetch.load();
     default: return -1;
   }
 }
 
 int b2g_plan_query(int kind, int M, int N, int K, int num_sms, int32_t* out, int out_len) {
-  if (out == nullptr || out_len < 9) return B2G_EINVAL;
+  if (out == nullptr || out_len < 10) return B2G_EINVAL;
   if (kind < B2G_KIND_F16 || kind > B2G_KIND_MXFP4 || M < 1 || N < 1 || K < 1 || num_sms < 2)
     return B2G_EINVAL;
   const Geometry g = geometry(kind, M, N, K, num_sms);
@@ -521,6 +568,7 @@ int b2g_plan_query(int kind, int M, int N, int K, int num_sms, int32_t* out, int
   out[6] = g.plan.sk_units;
   out[7] = g.launched;
   out[8] = g.plan.group_m;
+  out[9] = g.plan.splits;
   return B2G_OK;
 }
 
@@ -535,9 +583,9 @@ int b2g_plan_items(int kind, int M, int N, int K, int num_sms, int unit, int32_t
   int n = 0;
   while (cursor_next(g.plan, unit, cur, w)) {
     if (items != nullptr && n < max_items) {
-      int32_t* o = items + 8 * n;
-      o[0] = w.tile; o[1] = w.tm; o[2] = w.tn; o[3] = w.k_begin;
-      o[4] = w.k_end; o[5] = w.role; o[6] = w.first_contrib; o[7] = w.last_contrib;
+      int32_t* o = items + 9 * n;
+      o[0] = w.tile; o[1] = w.tm; o[2] = w.tn; o[3] = w.k_begin; o[4] = w.k_end;
+      o[5] = w.role; o[6] = w.first_contrib; o[7] = w.n_contrib; o[8] = w.contrib_stride;
     }
     ++n;
   }

@@ -8,17 +8,21 @@
 //
 // CTA layout (192 threads):
 //   warp 0      TMA producer: one thread fills a STAGES-deep shared-memory ring
-//               (A tile, B tile and, for block-scaled kinds, the E8M0 scales).
+//               (A tile, B tile and, for block-scaled kinds, the E8M0 scales,
+//               pre-arranged in 512-byte blocks by a relayout pass).
 //   warp 1      MMA issuer: allocates all 512 TMEM columns, one thread issues
 //               tcgen05.mma into a double-buffered TMEM accumulator and copies
 //               scale factors smem -> TMEM with tcgen05.cp.
-//   warps 2-5   epilogue: TMEM -> registers -> (stream-K fixup) -> bf16/fp16
+//   warps 2-5   epilogue: TMEM -> registers -> (split-tile fixup) -> bf16/fp16
 //               -> swizzled smem -> TMA store. Warp w reads TMEM lanes
 //               32*(w%4) .. 32*(w%4)+31.
 //
 // Tiles: cta_group::1 -> 128 x 256 per CTA; cta_group::2 -> 256 x 256 per CTA
 // pair, each CTA loading its own 128 rows of A and its own 128 rows of B (the
-// pair's MMA reads both halves; there is no multicast load anywhere).
+// pair's MMA reads both halves; there is no multicast load anywhere). With
+// block scales each CTA holds the scales of its own A rows and of all 256 B
+// rows (two 512-byte blocks per group), which the pair's tcgen05.cp copies
+// into each CTA's TMEM.
 //
 // Every K stage moves 128 bytes of K per row: 64 fp16/bf16, 128 e5m2 or 256
 // packed e2m1 elements, i.e. four MMAs of 32 bytes of K each.
@@ -49,22 +53,23 @@ struct alignas(64) GemmParams {
   CUtensorMap tmA;
   CUtensorMap tmB;
   CUtensorMap tmC;
-  const uint8_t* sfa;   // scales of A in the 512-byte blocked layout (scaled kinds)
-  const uint8_t* sfb;   // scales of B, same layout
-  float* partials;      // stream-K partial tiles, one 128 x 256 fp32 slot per CTA
-  uint32_t* flags;      // stream-K flags, one per (unit, CTA of pair, epilogue warp)
+  CUtensorMap tmSFA;    // blocked scales of A (u32 view: 128 words per 128-row group)
+  CUtensorMap tmSFB;    // blocked scales of B
+  float* partials;      // split-tile partials, one 128 x 256 fp32 slot per CTA
+  uint32_t* flags;      // split-tile flags, one per (unit, CTA of pair, epilogue warp)
   int* status;          // device status word, may be null
   SkPlan plan;
   int32_t M, N, K;
-  int32_t sf_groups;    // 4-scale groups per 128-row block in the blocked layout
-  int32_t inject;       // test hook: 1 = stream-K owners wait for a flag nobody raises
+  int32_t inject;       // test hook: 1 = split-tile owners wait for a flag nobody raises
+  int32_t prefetch;     // k-iterations the producer pulls into L2 ahead of its loads
   uint64_t timeout_ns;
 };
 
 template <int KIND>
 struct KindTraits {
   static constexpr bool kScaled = KIND == kKindMXE5M2 || KIND == kKindMXFP4;
-  // 4-scale groups (128 K elements of scales at 32 per scale) per stage.
+  // 4-scale groups (one 512-byte atom per 128 rows) per stage: a stage holds
+  // 128 bytes of K per row = 128 e5m2 (4 scales) or 256 e2m1 (8 scales).
   static constexpr int kGroupsPerStage = KIND == kKindMXFP4 ? 2 : 1;
   // a/b format field of the instruction descriptor.
   static constexpr uint32_t kFmt = KIND == kKindF16 ? 0u : 1u;
@@ -88,9 +93,11 @@ template <int KIND, int CG, int STAGES>
 struct SmemPlan {
   static constexpr bool kScaled = KindTraits<KIND>::kScaled;
   static constexpr int kGps = KindTraits<KIND>::kGroupsPerStage;
+  static constexpr uint32_t kThreads = 192;
   static constexpr uint32_t kABytes = 128 * 128;
   static constexpr uint32_t kBRows = CG == 1 ? 256 : 128;
   static constexpr uint32_t kBBytes = kBRows * 128;
+  // scales for this CTA's 128 A rows and all 256 B rows of the tile
   static constexpr uint32_t kSfaBytes = kScaled ? kGps * 512 : 0;
   static constexpr uint32_t kSfbBytes = kScaled ? 2 * kGps * 512 : 0;
   static constexpr uint32_t kEpiBufs = 2;
@@ -108,10 +115,11 @@ struct SmemPlan {
   static constexpr uint32_t kBytes = kMiscOff + 16;
   static constexpr uint32_t kDynBytes = kBytes + 1024;  // + alignment slack
 
-  // bytes landing per stage on the leader's full barrier (both CTAs of a pair)
+  // bytes the TMA lands per stage on the leader's full barrier (both CTAs)
   static constexpr uint32_t kTxBytes = CG * (kABytes + kBBytes + kSfaBytes + kSfbBytes);
 
-  // TMEM columns
+  // TMEM columns: two accumulators (overlapping by 32 columns when scale
+  // factors need room) and the scale-factor slots.
   static constexpr uint32_t kAccStride = kScaled ? 224 : 256;
   static constexpr uint32_t kSfaCol = 480;
   static constexpr uint32_t kSfbCol = 488;
@@ -145,7 +153,7 @@ __device__ __noinline__ bool wait_phase(uint32_t bar, uint32_t parity, volatile 
   }
 }
 
-// Bounded wait for a global stream-K flag to reach `want`.
+// Bounded wait for a global split-tile flag to reach `want`.
 __device__ __noinline__ bool wait_flag(const uint32_t* flag, uint32_t want,
                                        volatile uint32_t* abort_flag, const GemmParams& p,
                                        int site) {
@@ -229,6 +237,10 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ge
     prefetch_tensormap(&p.tmA);
     prefetch_tensormap(&p.tmB);
     prefetch_tensormap(&p.tmC);
+    if constexpr (kScaled) {
+      prefetch_tensormap(&p.tmSFA);
+      prefetch_tensormap(&p.tmSFB);
+    }
   }
   if (warp == 1) {
     tmem_alloc<CG>(smem_u32(tmem_slot), 512);
@@ -248,11 +260,31 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ge
       WorkCursor cur = cursor_begin(p.plan, unit);
       WorkItem w;
       bool alive = true;
+      // A second cursor runs `prefetch` k-iterations ahead and pulls those A/B
+      // boxes into L2 (off by default).
+      WorkCursor pf_cur = cur;
+      WorkItem pf_w;
+      bool pf_live = p.prefetch > 0 && cursor_next(p.plan, unit, pf_cur, pf_w);
+      int32_t pf_k = pf_live ? pf_w.k_begin : 0;
+      auto prefetch_one = [&]() {
+        while (pf_live && pf_k >= pf_w.k_end) {
+          pf_live = cursor_next(p.plan, unit, pf_cur, pf_w);
+          pf_k = pf_live ? pf_w.k_begin : 0;
+        }
+        if (!pf_live) return;
+        const int32_t ar = pf_w.tm * (128 * CG) + static_cast<int32_t>(rank) * 128;
+        const int32_t br = pf_w.tn * 256 + (CG == 2 ? static_cast<int32_t>(rank) * 128 : 0);
+        tma_prefetch_l2_2d(&p.tmA, pf_k * 128, ar);
+        tma_prefetch_l2_2d(&p.tmB, pf_k * 128, br);
+        ++pf_k;
+      };
+      for (int32_t i = 0; i < p.prefetch; ++i) prefetch_one();
       while (alive && cursor_next(p.plan, unit, cur, w)) {
         const int32_t a_row = w.tm * (128 * CG) + static_cast<int32_t>(rank) * 128;
         const int32_t b_row = w.tn * 256 + (CG == 2 ? static_cast<int32_t>(rank) * 128 : 0);
         for (int32_t k = w.k_begin; k < w.k_end; ++k, ++it) {
           const uint32_t s = it % STAGES, ph = (it / STAGES) & 1u;
+          if (p.prefetch > 0) prefetch_one();
           if (!wait_phase<false>(empty_bar(s), ph ^ 1u, abort_flag, p, B2G_SITE_EMPTY)) {
             alive = false;
             break;
@@ -270,18 +302,16 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ge
             tma_load_2d_pair(b_dst, &p.tmB, fb, kx, b_row);
           }
           if constexpr (kScaled) {
-            static_assert(CG == 1, "block-scaled kinds run with cta_group::1");
+            // blocked scales: this CTA's 128-row group of A, both groups of the B tile
             const uint32_t sfa_dst = sbase + SP::kSfaOff + s * SP::kSfaBytes;
             const uint32_t sfb_dst = sbase + SP::kSfbOff + s * SP::kSfbBytes;
-            const size_t g0 = static_cast<size_t>(k) * kGps;
-            const uint8_t* sa =
-                p.sfa + (static_cast<size_t>(a_row >> 7) * p.sf_groups + g0) * 512u;
-            bulk_load(sfa_dst, sa, kGps * 512u, fb);
-#pragma unroll
-            for (int rb = 0; rb < 2; ++rb) {
-              const uint8_t* sb =
-                  p.sfb + (static_cast<size_t>(w.tn * 2 + rb) * p.sf_groups + g0) * 512u;
-              bulk_load(sfb_dst + rb * kGps * 512u, sb, kGps * 512u, fb);
+            const int32_t sx = k * kGps * 128;
+            if constexpr (CG == 1) {
+              tma_load_2d(sfa_dst, &p.tmSFA, fb, sx, a_row >> 7);
+              tma_load_2d(sfb_dst, &p.tmSFB, fb, sx, w.tn * 2);
+            } else {
+              tma_load_2d_pair(sfa_dst, &p.tmSFA, fb, sx, a_row >> 7);
+              tma_load_2d_pair(sfb_dst, &p.tmSFB, fb, sx, w.tn * 2);
             }
           }
         }
@@ -315,7 +345,7 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ge
         const uint32_t d_tmem = tmem_base + b * SP::kAccStride;
         for (int32_t k = w.k_begin; k < w.k_end; ++k, ++it) {
           const uint32_t s = it % STAGES, ph = (it / STAGES) & 1u;
-          if (!wait_phase<false>(full_bar(s), ph, abort_flag, p, B2G_SITE_FULL)) {
+          if (!wait_phase<CG == 2>(full_bar(s), ph, abort_flag, p, B2G_SITE_FULL)) {
             alive = false;
             break;
           }
@@ -325,6 +355,7 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ge
           const uint64_t adesc = sdesc_kmajor_sw128(a_addr);
           const uint64_t bdesc = sdesc_kmajor_sw128(b_addr);
           if constexpr (kScaled) {
+            // scale factors of this stage: smem -> TMEM (in issue order with the MMAs)
             const uint32_t sfa_addr = sbase + SP::kSfaOff + s * SP::kSfaBytes;
             const uint32_t sfb_addr = sbase + SP::kSfbOff + s * SP::kSfbBytes;
 #pragma unroll
@@ -391,6 +422,7 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ge
       const uint32_t tbase = tmem_base + ((quad * 32u) << 16) + b * SP::kAccStride;
       const int32_t m0 = w.tm * (128 * CG) + static_cast<int32_t>(rank) * 128 + quad * 32;
       const int32_t n0 = w.tn * 256;
+      // with overlapping accumulators the shared 32 columns are drained first
       const uint32_t first_chunk = kScaled ? (b == 0 ? 7u : 0u) : 0u;
       bool contribs_ready = w.role != kRoleOwner;
       bool failed = false;
@@ -425,7 +457,8 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ge
         if (w.role == kRoleOwner) {
           if (!contribs_ready) {
             bool fok = true;
-            for (int32_t u2 = w.first_contrib; u2 <= w.last_contrib && fok; ++u2)
+            for (int32_t ci2 = 0, u2 = w.first_contrib; ci2 < w.n_contrib && fok;
+                 ++ci2, u2 += w.contrib_stride)
               fok = wait_flag(p.flags + flag_index(u2, rank, quad, CG), p.inject ? 2u : 1u,
                               abort_flag, p, B2G_SITE_FLAG);
             fok = __all_sync(0xffffffffu, fok);
@@ -435,21 +468,30 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ge
             }
             contribs_ready = true;
           }
-          for (int32_t u2 = w.first_contrib; u2 <= w.last_contrib; ++u2) {
+          for (int32_t ci2 = 0, u2 = w.first_contrib; ci2 < w.n_contrib;
+               ++ci2, u2 += w.contrib_stride) {
             const float4* src = reinterpret_cast<const float4*>(
                 p.partials + partial_slot(u2, rank, CG) + static_cast<size_t>(row) * 256u +
                 c * 32u);
+            float4 t[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) t[i] = __ldcg(src + i);
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-              const float4 t = __ldcg(src + i);
-              v[4 * i + 0] = __float_as_uint(__uint_as_float(v[4 * i + 0]) + t.x);
-              v[4 * i + 1] = __float_as_uint(__uint_as_float(v[4 * i + 1]) + t.y);
-              v[4 * i + 2] = __float_as_uint(__uint_as_float(v[4 * i + 2]) + t.z);
-              v[4 * i + 3] = __float_as_uint(__uint_as_float(v[4 * i + 3]) + t.w);
+              v[4 * i + 0] = __float_as_uint(__uint_as_float(v[4 * i + 0]) + t[i].x);
+              v[4 * i + 1] = __float_as_uint(__uint_as_float(v[4 * i + 1]) + t[i].y);
+              v[4 * i + 2] = __float_as_uint(__uint_as_float(v[4 * i + 2]) + t[i].z);
+              v[4 * i + 3] = __float_as_uint(__uint_as_float(v[4 * i + 3]) + t[i].w);
             }
           }
         }
-        // Convert and stage 32 rows x 32 columns in the 64-byte swizzle.
+        // Convert and stage 32 rows x 32 columns in the 64-byte swizzle, then
+        // one TMA store per warp (the tensor map clips rows / columns past C).
+        // Chunks wholly outside C are skipped without touching the staging
+        // buffers, which alternate per store actually issued: the buffer being
+        // written is never the one the newest store may still be reading.
+        const int32_t x = n0 + static_cast<int32_t>(c * 32u);
+        if (x >= p.N || m0 >= p.M) continue;
         uint8_t* buf = stage_base + (nstore & 1u) * SP::kEpiBufBytes;
         if (lane == 0) bulk_wait_group_read<1>();
         __syncwarp();
@@ -465,8 +507,7 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ge
         }
         fence_proxy_async_smem();
         __syncwarp();
-        const int32_t x = n0 + static_cast<int32_t>(c * 32u);
-        if (lane == 0 && x < p.N && m0 < p.M) {
+        if (lane == 0) {
           tma_store_2d(&p.tmC, smem_u32(buf), x, m0);
           bulk_commit_group();
         }
@@ -480,7 +521,8 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ge
       } else if (w.role == kRoleOwner) {
         __syncwarp();
         if (lane == 0)
-          for (int32_t u2 = w.first_contrib; u2 <= w.last_contrib; ++u2)
+          for (int32_t ci2 = 0, u2 = w.first_contrib; ci2 < w.n_contrib;
+               ++ci2, u2 += w.contrib_stride)
             p.flags[flag_index(u2, rank, quad, CG)] = 0u;
       }
       tc_fence_before();

@@ -1,5 +1,5 @@
 // Quantise-and-pack kernels for the low-precision operands, and the relayout
-// of E8M0 scales into the layout tcgen05.cp copies into TMEM.
+// of E8M0 scales into the blocked layout the GEMM's TMA loads.
 //
 // The reference has no quantiser: its bench draws random packed nibbles and
 // random scale bytes (kernels/gemm/intra_wave/a4w4/bench.py:115-146) and casts
@@ -182,24 +182,36 @@ __global__ void cast_e5m2_kernel(const T* __restrict__ src, int64_t n, uint8_t* 
     dst[i] = static_cast<uint8_t>(e5m2_from_f32(to_f32<T>(src[i])));
 }
 
-// -------------------------------------------------------- scale relayout --
-// (rows, K/32) E8M0 bytes of any strides -> 512-byte blocks, one per 128-row
-// block rb and 4-scale group g, at ((rb * groups) + g) * 512, laid out so that
-// byte r0 * 16 + r1 * 4 + j holds the scale of row rb*128 + r1*32 + r0 for
-// k-block 4g + j. This is the 32-lane x 128-bit source a tcgen05.cp 32x128b
-// (warpx4) copy turns into the TMEM scale-factor layout of a 128-row operand.
-// Rows or k-blocks past the end are filled with 127 (scale 1.0).
-__global__ void sf_relayout_kernel(const uint8_t* __restrict__ src, int64_t s0, int64_t s1,
-                                   int32_t rows, int32_t kscales, int32_t row_blocks,
-                                   int32_t groups, uint8_t* __restrict__ dst) {
-  const int64_t total = static_cast<int64_t>(row_blocks) * groups * 32;
+
+// ------------------------------------------------------- scale relayout --
+// (rows, K/32) E8M0 bytes of any strides -> blocked layout: for 128-row block
+// rb and 4-scale group g, 512 bytes at (rb * groups + g) * 512 where byte
+// r0 * 16 + r1 * 4 + j holds the scale of row rb*128 + r1*32 + r0, k-block
+// 4g + j. That is the 32 lanes x 16 bytes source of a 32x128b (warpx4)
+// tcgen05.cp, which spreads it into the TMEM scale-factor layout of a
+// 128-row operand. Positions past the matrix hold 127 (scale 1.0). One launch
+// converts both operands: threads [0, n_a) do A, the rest B.
+struct RelayoutArgs {
+  const uint8_t* src;
+  int64_t s0, s1;
+  int32_t rows, row_blocks;
+  uint8_t* dst;
+};
+
+__global__ void sf_relayout_kernel(RelayoutArgs a, RelayoutArgs b, int32_t kscales,
+                                   int32_t groups) {
+  const int64_t n_a = static_cast<int64_t>(a.row_blocks) * groups * 32;
+  const int64_t total = n_a + static_cast<int64_t>(b.row_blocks) * groups * 32;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
        i += stride) {
-    const int32_t r0 = static_cast<int32_t>(i & 31);
-    const int64_t t = i >> 5;
-    const int32_t g = static_cast<int32_t>(t % groups);
-    const int64_t rb = t / groups;
+    const bool is_a = i < n_a;
+    const RelayoutArgs& t = is_a ? a : b;
+    const int64_t li = is_a ? i : i - n_a;
+    const int32_t r0 = static_cast<int32_t>(li & 31);
+    const int64_t q = li >> 5;
+    const int32_t g = static_cast<int32_t>(q % groups);
+    const int64_t rb = q / groups;
     uint32_t w[4];
 #pragma unroll
     for (int r1 = 0; r1 < 4; ++r1) {
@@ -208,12 +220,13 @@ __global__ void sf_relayout_kernel(const uint8_t* __restrict__ src, int64_t s0, 
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int32_t k = g * 4 + j;
-        const uint32_t v = (row < rows && k < kscales) ? src[row * s0 + k * s1] : 127u;
+        const uint32_t v =
+            (row < t.rows && k < kscales) ? __ldg(t.src + row * t.s0 + k * t.s1) : 127u;
         word |= v << (8 * j);
       }
       w[r1] = word;
     }
-    *reinterpret_cast<uint4*>(dst + (rb * groups + g) * 512 + r0 * 16) =
+    *reinterpret_cast<uint4*>(t.dst + (rb * groups + g) * 512 + r0 * 16) =
         make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
@@ -260,11 +273,17 @@ cudaError_t launch_cast_e5m2(const void* src, int dtype, int64_t n, uint8_t* dst
   return cudaGetLastError();
 }
 
-cudaError_t launch_sf_relayout(const uint8_t* src, int64_t s0, int64_t s1, int rows, int kscales,
-                               int row_blocks, int groups, uint8_t* dst, cudaStream_t stream) {
-  const int64_t work = static_cast<int64_t>(row_blocks) * groups * 32;
-  sf_relayout_kernel<<<grid_for(work, 256), 256, 0, stream>>>(src, s0, s1, rows, kscales,
-                                                              row_blocks, groups, dst);
+cudaError_t launch_sf_relayout(const uint8_t* sa, int64_t sa0, int64_t sa1, int rows_a,
+                               uint8_t* dst_a, const uint8_t* sb, int64_t sb0, int64_t sb1,
+                               int rows_b, uint8_t* dst_b, int kscales, cudaStream_t stream) {
+  const int32_t groups = (kscales + 3) / 4;
+  RelayoutArgs a{sa, sa0, sa1, rows_a, (rows_a + 127) / 128, dst_a};
+  RelayoutArgs b{sb, sb0, sb1, rows_b, (rows_b + 127) / 128, dst_b};
+  if (sa == nullptr) a.row_blocks = 0;
+  if (sb == nullptr) b.row_blocks = 0;
+  const int64_t work = (static_cast<int64_t>(a.row_blocks) + b.row_blocks) * groups * 32;
+  if (work == 0) return cudaSuccess;
+  sf_relayout_kernel<<<grid_for(work, 256), 256, 0, stream>>>(a, b, kscales, groups);
   return cudaGetLastError();
 }
 

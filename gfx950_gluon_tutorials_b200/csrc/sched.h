@@ -8,12 +8,19 @@
 // pair (cta_group::2); a unit walks its tiles in the same GROUP_M-swizzled
 // raster so concurrently running units share A and B panels in L2.
 //
-// Stream-K ownership rule: the unit that runs k-iteration 0 of a split tile
+// Two ways to spread the tiles left after the full data-parallel waves:
+//   stream-K (modes 1, 2): their (tile, k) iteration space is cut into equal
+//     contiguous ranges, one per unit;
+//   split (mode 3): every leftover tile is cut into S equal k-chunks and chunk
+//     s of leftover tile j goes to unit s * leftover + j, so units running at
+//     the same time stream the same k-range of neighbouring tiles (their A and
+//     B panels stay shared in L2, which contiguous ranges lose).
+// Ownership rule (both): the unit that runs k-iteration 0 of a split tile
 // owns it. Every other unit touching the tile does so in the FIRST segment of
 // its range, writes an fp32 partial to its own workspace slot and raises a
 // flag; the owner adds the partials in increasing unit order (deterministic)
-// after its own accumulation and stores C. Contributors never wait, so the
-// waits cannot form a cycle.
+// after its own accumulation and stores C. Contributors never wait and always
+// have larger unit numbers than the owner, so the waits cannot form a cycle.
 #pragma once
 
 #include <stdint.h>
@@ -33,9 +40,10 @@ struct SkPlan {
   int32_t k_iters;           // k-iterations (pipeline stages) per tile
   int32_t units;             // persistent work units launched
   int32_t dp_tiles;          // tiles [0, dp_tiles) are data-parallel
-  int32_t sk_units;          // units [0, sk_units) share the stream-K iterations
+  int32_t sk_units;          // units [0, sk_units) share the leftover tiles
   int64_t sk_iters;          // (tiles - dp_tiles) * k_iters
   int32_t group_m;           // raster group height in tiles
+  int32_t splits;            // split mode: k-chunks per leftover tile (0 = stream-K)
 };
 
 struct WorkItem {
@@ -44,7 +52,8 @@ struct WorkItem {
   int32_t k_begin;   // first k-iteration (inclusive)
   int32_t k_end;     // last k-iteration (exclusive)
   int32_t role;      // kRoleFull / kRoleOwner / kRoleContrib
-  int32_t first_contrib, last_contrib;  // owner only: contributing units [first, last]
+  // owner only: contributing units first, first + stride, ... (n_contrib of them)
+  int32_t first_contrib, n_contrib, contrib_stride;
 };
 
 B2G_HD int32_t plan_tiles(const SkPlan& p) { return p.tiles_m * p.tiles_n; }
@@ -64,9 +73,10 @@ B2G_HD int64_t sk_range_begin(const SkPlan& p, int32_t u) {
   return (p.sk_iters * u) / p.sk_units;
 }
 
-// Builds the plan. `sk_mode`: 0 = no stream-K (all tiles data-parallel, the
+// Builds the plan. `sk_mode`: 0 = no splitting (all tiles data-parallel, the
 // last wave partial); 1 = stream-K over the partial last wave only;
-// 2 = stream-K over the last full wave plus the partial one.
+// 2 = stream-K over the last full wave plus the partial one; 3 = split the
+// tiles of the partial last wave into equal k-chunks.
 inline SkPlan make_plan(int32_t tiles_m, int32_t tiles_n, int32_t k_iters, int32_t units,
                         int32_t group_m, int32_t sk_mode, int32_t min_sk_iters) {
   SkPlan p{};
@@ -75,6 +85,7 @@ inline SkPlan make_plan(int32_t tiles_m, int32_t tiles_n, int32_t k_iters, int32
   p.k_iters = k_iters;
   p.units = units;
   p.group_m = group_m < 1 ? 1 : group_m;
+  if (min_sk_iters < 1) min_sk_iters = 1;
   const int32_t tiles = tiles_m * tiles_n;
   int32_t dp = tiles;
   if (sk_mode != 0 && tiles % units != 0) {
@@ -83,16 +94,24 @@ inline SkPlan make_plan(int32_t tiles_m, int32_t tiles_n, int32_t k_iters, int32
     dp = waves * units;
   }
   p.dp_tiles = dp;
-  p.sk_iters = static_cast<int64_t>(tiles - dp) * k_iters;
-  if (p.sk_iters > 0) {
-    if (min_sk_iters < 1) min_sk_iters = 1;
-    int64_t su = p.sk_iters / min_sk_iters;
-    if (su > units) su = units;
-    if (su < 1) su = 1;
-    p.sk_units = static_cast<int32_t>(su);
-  } else {
-    p.sk_units = 0;
+  const int32_t left = tiles - dp;
+  p.sk_iters = static_cast<int64_t>(left) * k_iters;
+  p.sk_units = 0;
+  p.splits = 0;
+  if (left == 0) return p;
+  if (sk_mode == 3) {
+    int32_t s = units / left;
+    const int32_t s_max = k_iters / min_sk_iters;
+    if (s > s_max) s = s_max;
+    if (s < 1) s = 1;
+    p.splits = s;
+    p.sk_units = left * s;
+    return p;
   }
+  int64_t su = p.sk_iters / min_sk_iters;
+  if (su > units) su = units;
+  if (su < 1) su = 1;
+  p.sk_units = static_cast<int32_t>(su);
   return p;
 }
 
@@ -117,17 +136,40 @@ B2G_HD WorkCursor cursor_begin(const SkPlan& p, int32_t u) {
 }
 
 B2G_HD bool cursor_next(const SkPlan& p, int32_t u, WorkCursor& c, WorkItem& w) {
+  w.first_contrib = -1;
+  w.n_contrib = 0;
+  w.contrib_stride = 1;
   if (c.dp_next < p.dp_tiles) {
     w.tile = c.dp_next;
     w.k_begin = 0;
     w.k_end = p.k_iters;
     w.role = kRoleFull;
-    w.first_contrib = w.last_contrib = -1;
     c.dp_next += p.units;
     tile_coords(p, w.tile, w.tm, w.tn);
     return true;
   }
   if (c.sk_pos >= c.sk_end) return false;
+  if (p.splits > 0) {
+    // split mode: exactly one chunk per unit
+    const int32_t left = p.sk_units / p.splits;
+    const int32_t j = u % left, s = u / left;
+    w.tile = p.dp_tiles + j;
+    w.k_begin = static_cast<int32_t>((static_cast<int64_t>(p.k_iters) * s) / p.splits);
+    w.k_end = static_cast<int32_t>((static_cast<int64_t>(p.k_iters) * (s + 1)) / p.splits);
+    if (p.splits == 1) {
+      w.role = kRoleFull;
+    } else if (s == 0) {
+      w.role = kRoleOwner;
+      w.first_contrib = u + left;
+      w.n_contrib = p.splits - 1;
+      w.contrib_stride = left;
+    } else {
+      w.role = kRoleContrib;
+    }
+    c.sk_pos = c.sk_end;
+    tile_coords(p, w.tile, w.tm, w.tn);
+    return true;
+  }
   const int64_t local_tile = c.sk_pos / p.k_iters;
   const int64_t tile_begin = local_tile * p.k_iters;
   const int64_t tile_end = tile_begin + p.k_iters;
@@ -135,7 +177,6 @@ B2G_HD bool cursor_next(const SkPlan& p, int32_t u, WorkCursor& c, WorkItem& w) 
   w.tile = p.dp_tiles + static_cast<int32_t>(local_tile);
   w.k_begin = static_cast<int32_t>(c.sk_pos - tile_begin);
   w.k_end = static_cast<int32_t>(seg_end - tile_begin);
-  w.first_contrib = w.last_contrib = -1;
   if (w.k_begin > 0) {
     w.role = kRoleContrib;
   } else if (w.k_end == p.k_iters) {
@@ -145,7 +186,7 @@ B2G_HD bool cursor_next(const SkPlan& p, int32_t u, WorkCursor& c, WorkItem& w) 
     int32_t v = u + 1;
     w.first_contrib = v;
     while (v < p.sk_units && sk_range_begin(p, v) < tile_end) ++v;
-    w.last_contrib = v - 1;
+    w.n_contrib = v - w.first_contrib;
   }
   c.sk_pos = seg_end;
   tile_coords(p, w.tile, w.tm, w.tn);

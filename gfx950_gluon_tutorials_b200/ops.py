@@ -169,14 +169,11 @@ def gemm_f8(a: torch.Tensor, b_t: torch.Tensor, c: torch.Tensor | None = None,
     cv, copy_back = _c_view(c)
     scaled = a_scales is not None
     kind = _lib.KIND_MXE5M2 if scaled else _lib.KIND_E5M2
-    if scaled:
-        _check_scales(a_scales, M, K, "a_scales")
-        _check_scales(b_scales, N, K, "b_scales")
+    sa = _scale_args(a_scales, M, K, "a_scales") if scaled else (None, 0, 0)
+    sb = _scale_args(b_scales, N, K, "b_scales") if scaled else (None, 0, 0)
     ws = workspace(lib().b2g_gemm_workspace_bytes(kind, M, N, K), dev)
     rc = lib().b2g_gemm_f8(
-        a_.data_ptr(), a_.stride(0), b_.data_ptr(), b_.stride(0),
-        _ptr(a_scales), a_scales.stride(0) if scaled else 0, a_scales.stride(1) if scaled else 0,
-        _ptr(b_scales), b_scales.stride(0) if scaled else 0, b_scales.stride(1) if scaled else 0,
+        a_.data_ptr(), a_.stride(0), b_.data_ptr(), b_.stride(0), *sa, *sb,
         cv.data_ptr(), cv.stride(0), M, N, K, _OUT_DT[c.dtype], ws.data_ptr(), ws.numel(),
         status_tensor(dev).data_ptr(), _stream_handle(dev))
     check(rc, "b2g_gemm_f8")
@@ -185,7 +182,49 @@ def gemm_f8(a: torch.Tensor, b_t: torch.Tensor, c: torch.Tensor | None = None,
     return c
 
 
+class BlockedScales:
+    """E8M0 scales already in the GEMM's blocked layout (see ``block_scales``).
+
+    Passing these instead of a (rows, K/32) tensor skips the per-call relayout,
+    which is worth it for static operands such as weights."""
+
+    def __init__(self, data: torch.Tensor, rows: int, K: int):
+        self.data, self.rows, self.K = data, rows, K
+
+    @property
+    def is_cuda(self) -> bool:
+        return self.data.is_cuda
+
+    @property
+    def device(self) -> torch.device:
+        return self.data.device
+
+
+def block_scales(s: torch.Tensor, K: int | None = None) -> BlockedScales:
+    """(rows, K/32) E8M0 scales of any strides -> BlockedScales (one launch)."""
+    dev = _require_cuda(s)
+    rows, kb = s.shape
+    K = K if K is not None else kb * 32
+    out = torch.empty(lib().b2g_scales_blocked_bytes(rows, K), dtype=torch.uint8, device=dev)
+    check(lib().b2g_scales_to_blocked(s.data_ptr(), s.stride(0), s.stride(1), rows, K,
+                                      out.data_ptr(), _stream_handle(dev)),
+          "b2g_scales_to_blocked")
+    return BlockedScales(out, rows, K)
+
+
+def _scale_args(s, rows: int, K: int, name: str) -> tuple[int, int, int]:
+    """(pointer, s0, s1) for a scale operand; blocked scales pass strides (0, 0)."""
+    if isinstance(s, BlockedScales):
+        if (s.rows, s.K) != (rows, K):
+            raise ValueError(f"{name} was blocked for ({s.rows}, K={s.K}), need ({rows}, K={K})")
+        return s.data.data_ptr(), 0, 0
+    _check_scales(s, rows, K, name)
+    return s.data_ptr(), s.stride(0), s.stride(1)
+
+
 def _check_scales(s: torch.Tensor, rows: int, K: int, name: str) -> None:
+    if isinstance(s, BlockedScales):
+        return
     if s.dtype != torch.uint8 or not s.is_cuda:
         raise ValueError(f"{name} must be a CUDA uint8 (E8M0) tensor")
     if tuple(s.shape) != (rows, K // 32):
@@ -197,7 +236,7 @@ def gemm_mxf4(a: torch.Tensor, b_t: torch.Tensor, a_scales: torch.Tensor,
               out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
     """C = dequant(A) @ dequant(B_t)^T for packed e2m1 A (M, K/2), B_t (N, K/2)
     and E8M0 scales a_scales (M, K/32), b_scales (N, K/32) of any strides."""
-    dev = _require_cuda(a, b_t, a_scales, b_scales)
+    dev = _require_cuda(a, b_t)
     if a.dtype != torch.uint8 or b_t.dtype != torch.uint8:
         raise ValueError("a4w4 operands are packed uint8")
     M, Kp = a.shape
@@ -205,16 +244,14 @@ def gemm_mxf4(a: torch.Tensor, b_t: torch.Tensor, a_scales: torch.Tensor,
     if Kp != Kp2:
         raise ValueError("Incompatible dimensions")
     K = 2 * Kp
-    _check_scales(a_scales, M, K, "a_scales")
-    _check_scales(b_scales, N, K, "b_scales")
+    sa = _scale_args(a_scales, M, K, "a_scales")
+    sb = _scale_args(b_scales, N, K, "b_scales")
     c = _out(c, M, N, c.dtype if c is not None else out_dtype, dev)
     a_, b_ = _k_major(a), _k_major(b_t)
     cv, copy_back = _c_view(c)
     ws = workspace(lib().b2g_gemm_workspace_bytes(_lib.KIND_MXFP4, M, N, K), dev)
     rc = lib().b2g_gemm_mxf4(
-        a_.data_ptr(), a_.stride(0), b_.data_ptr(), b_.stride(0),
-        a_scales.data_ptr(), a_scales.stride(0), a_scales.stride(1),
-        b_scales.data_ptr(), b_scales.stride(0), b_scales.stride(1),
+        a_.data_ptr(), a_.stride(0), b_.data_ptr(), b_.stride(0), *sa, *sb,
         cv.data_ptr(), cv.stride(0), M, N, K, _OUT_DT[c.dtype], ws.data_ptr(), ws.numel(),
         status_tensor(dev).data_ptr(), _stream_handle(dev))
     check(rc, "b2g_gemm_mxf4")
@@ -278,24 +315,26 @@ def cast_e5m2(x: torch.Tensor) -> torch.Tensor:
 
 def plan(kind: int, M: int, N: int, K: int, num_sms: int = 148) -> dict:
     """Host-side schedule summary (no GPU needed)."""
-    out = (ctypes.c_int32 * 9)()
-    check(lib().b2g_plan_query(kind, M, N, K, num_sms, out, 9), "b2g_plan_query")
+    out = (ctypes.c_int32 * 10)()
+    check(lib().b2g_plan_query(kind, M, N, K, num_sms, out, 10), "b2g_plan_query")
     keys = ("cta_group", "tiles_m", "tiles_n", "k_iters", "units", "dp_tiles", "sk_units",
-            "launched", "group_m")
+            "launched", "group_m", "splits")
     return dict(zip(keys, list(out)))
 
 
 def plan_items(kind: int, M: int, N: int, K: int, unit: int, num_sms: int = 148) -> list[tuple]:
-    """Work items (tile, tm, tn, k_begin, k_end, role, first, last) of one unit."""
+    """Work items (tile, tm, tn, k_begin, k_end, role, first_contrib, n_contrib,
+    contrib_stride) of one unit."""
     n = lib().b2g_plan_items(kind, M, N, K, num_sms, unit, None, 0)
     if n < 0:
         check(n, "b2g_plan_items")
-    buf = (ctypes.c_int32 * (8 * max(n, 1)))()
+    buf = (ctypes.c_int32 * (9 * max(n, 1)))()
     lib().b2g_plan_items(kind, M, N, K, num_sms, unit, buf, n)
-    return [tuple(buf[8 * i:8 * i + 8]) for i in range(n)]
+    return [tuple(buf[9 * i:9 * i + 9]) for i in range(n)]
 
 
 __all__ = [
-    "B2GError", "gemm_f16", "gemm_f8", "gemm_mxf4", "quantize_mxfp4", "quantize_mxe5m2",
+    "B2GError", "BlockedScales", "block_scales", "gemm_f16", "gemm_f8", "gemm_mxf4",
+    "quantize_mxfp4", "quantize_mxe5m2",
     "cast_e5m2", "workspace", "status_tensor", "check_status", "plan", "plan_items",
 ]

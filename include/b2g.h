@@ -107,7 +107,10 @@ B2G_API int b2g_gemm_f16(const void* A, int64_t lda, const void* B, int64_t ldb,
  * is unscaled (the reference's a8w8 contract, usually out_dtype = fp16).
  * Otherwise both scale tensors are E8M0 bytes of logical shape (rows, K/32)
  * with element strides (s0, s1) - any order, e.g. the reference's
- * M-contiguous (1, rows_pad) - and K must be a multiple of 32. */
+ * M-contiguous (1, rows_pad) - and K must be a multiple of 32. Such scales are
+ * relaid into the workspace by an extra launch on `stream`; strides (0, 0)
+ * instead mean the pointer already holds the blocked layout written by
+ * b2g_scales_to_blocked (16-byte aligned), and that tensor is used as is. */
 B2G_API int b2g_gemm_f8(const void* A, int64_t lda, const void* B, int64_t ldb, const uint8_t* sfa,
                 int64_t sfa_s0, int64_t sfa_s1, const uint8_t* sfb, int64_t sfb_s0,
                 int64_t sfb_s1, void* C, int64_t ldc, int M, int N, int K, int out_dtype,
@@ -121,6 +124,15 @@ B2G_API int b2g_gemm_mxf4(const uint8_t* A, int64_t lda, const uint8_t* B, int64
                   int64_t sfb_s0, int64_t sfb_s1, void* C, int64_t ldc, int M, int N, int K,
                   int out_dtype, void* workspace, size_t workspace_bytes, int* status,
                   void* stream);
+
+/* Blocked E8M0 scale layout: for each 128-row block and each group of 4
+ * k-blocks (4 scales), 512 bytes in which byte r0*16 + r1*4 + j holds the
+ * scale of row 128*block + 32*r1 + r0 for k-block 4*group + j; blocks are
+ * stored row-block major. Positions past the matrix hold 127. Static operands
+ * (weights) can be converted once and passed with strides (0, 0). */
+B2G_API size_t b2g_scales_blocked_bytes(int rows, int K);
+B2G_API int b2g_scales_to_blocked(const uint8_t* src, int64_t s0, int64_t s1, int rows, int K,
+                                  uint8_t* dst, void* stream);
 
 /* Quantise fp32 `src` (rows x K, row stride ld) to MXFP4: per row and 32-K
  * block, scale exponent s = floor(log2(max|x|)) - 2 (E8M0 byte s + 127,
@@ -145,29 +157,35 @@ B2G_API int b2g_cast_e5m2(const void* src, int src_dtype, int64_t n, uint8_t* ds
 /* ---- process-wide tuning and test options (b2g_set_option keys) ----
  * They change how later launches are planned; set them before computing a
  * workspace size and do not change them while GEMMs are in flight. */
-#define B2G_OPT_PAIR 1        /* 1 (default): cta_group::2 CTA pairs for f16/bf16/e5m2 */
-#define B2G_OPT_SK_MODE 2     /* 0: data-parallel only; 1 (default): stream-K over the
-                                 partial last wave; 2: stream-K over the last full
-                                 wave plus the partial one */
-#define B2G_OPT_GROUP_M 3     /* raster group height in tiles (default 8) */
+#define B2G_OPT_PAIR 1        /* 1 (default): cta_group::2 CTA pairs (256 x 256 tiles);
+                                 0: one CTA per tile (128 x 256) */
+#define B2G_OPT_SK_MODE 2     /* tiles left after the full data-parallel waves:
+                                 0: run as a partial wave; 1: stream-K (equal
+                                 contiguous (tile, k) ranges per unit); 2: stream-K
+                                 over the last full wave plus the partial one;
+                                 3 (default): split each into equal k-chunks */
+#define B2G_OPT_GROUP_M 3     /* raster group height in tiles (default 1: row-major) */
 #define B2G_OPT_MIN_SK_ITERS 4 /* minimum k-iterations per stream-K unit (default 4) */
 #define B2G_OPT_TIMEOUT_MS 5  /* bounded-wait deadline in ms (default 2000) */
 #define B2G_OPT_INJECT_FLAG_TIMEOUT 6 /* test hook: stream-K owners wait for a flag
                                          value no contributor writes, so the wait
                                          expires and the status word is set */
 #define B2G_OPT_MAX_UNITS 7   /* cap on persistent work units (0 = one per SM / pair) */
+#define B2G_OPT_L2_PREFETCH 8 /* k-iterations of A/B the producer pulls into L2 ahead
+                                 of its shared-memory loads (default 0 = off) */
 
 B2G_API int b2g_set_option(int key, int64_t value);
 B2G_API int64_t b2g_get_option(int key);
 
 /* Host-only view of the persistent schedule for a device with `num_sms` SMs
- * (no GPU needed). out[0..8] = {cta_group, tiles_m, tiles_n, k_iters, units,
- * dp_tiles, sk_units, launched_units, group_m}. */
+ * (no GPU needed). out[0..9] = {cta_group, tiles_m, tiles_n, k_iters, units,
+ * dp_tiles, sk_units, launched_units, group_m, splits}. */
 B2G_API int b2g_plan_query(int kind, int M, int N, int K, int num_sms, int32_t* out, int out_len);
 
-/* Work items of one unit in execution order, 8 ints each: {tile, tm, tn,
- * k_begin, k_end, role (0 full, 1 stream-K owner, 2 contributor),
- * first_contrib, last_contrib}. Returns the item count (items may be NULL). */
+/* Work items of one unit in execution order, 9 ints each: {tile, tm, tn,
+ * k_begin, k_end, role (0 full, 1 split-tile owner, 2 contributor),
+ * first_contrib, n_contrib, contrib_stride}. Returns the item count (items may
+ * be NULL). */
 B2G_API int b2g_plan_items(int kind, int M, int N, int K, int num_sms, int unit, int32_t* items,
                    int max_items);
 

@@ -42,12 +42,15 @@ def assert_close(c: np.ndarray, ref: np.ndarray, tol: float, ref_atol: bool = Tr
 
 
 @pytest.fixture(params=[
+    dict(pair=1, sk=3, min_sk=4, units=0),
+    dict(pair=0, sk=3, min_sk=4, units=0),
     dict(pair=1, sk=1, min_sk=4, units=0),
     dict(pair=0, sk=1, min_sk=4, units=0),
     dict(pair=1, sk=2, min_sk=1, units=0),
     dict(pair=0, sk=0, min_sk=4, units=0),
     dict(pair=1, sk=1, min_sk=1, units=5),   # few units: deep stream-K splits
     dict(pair=0, sk=2, min_sk=1, units=7),
+    dict(pair=1, sk=3, min_sk=1, units=9),
 ], ids=lambda d: f"pair{d['pair']}-sk{d['sk']}-min{d['min_sk']}-u{d['units']}")
 def sched(request, cuda_device):
     keys = {"pair": _lib.OPT_PAIR, "sk": _lib.OPT_SK_MODE, "min_sk": _lib.OPT_MIN_SK_ITERS,
@@ -271,3 +274,50 @@ def test_repeated_calls_are_deterministic(cuda_device):
         ops.check_status()
     finally:
         _lib.set_option(_lib.OPT_MIN_SK_ITERS, old)
+
+
+@pytest.mark.parametrize("layout", ["m_contig", "k_contig", "strided", "odd_k"])
+@pytest.mark.parametrize("pair", [1, 0])
+def test_a4w4_scale_layouts(cuda_device, layout, pair):
+    """Scales of any strides: row-contiguous (the reference's storage), K-contiguous,
+    a strided view, and a K/32 that is not a multiple of 4 (byte gathers)."""
+    M, N, K = (300, 520, 1024) if layout != "odd_k" else (256, 384, 192)
+    a, b, sa, sb = _reference_style_mxfp4(M, N, K, 17)
+    if layout == "k_contig":
+        sa, sb = sa.contiguous(), sb.contiguous()
+    elif layout == "strided":
+        big_a = torch.full((M, 2 * (K // 32)), 255, dtype=torch.uint8, device="cuda")
+        big_b = torch.full((N, 2 * (K // 32)), 255, dtype=torch.uint8, device="cuda")
+        big_a[:, ::2] = sa
+        big_b[:, ::2] = sb
+        sa, sb = big_a[:, ::2], big_b[:, ::2]
+    elif layout == "odd_k":
+        sa = sa.contiguous()
+    old = _lib.get_option(_lib.OPT_PAIR)
+    _lib.set_option(_lib.OPT_PAIR, pair)
+    try:
+        c = a4w4.matmul(a, b, sa, sb)
+        ops.check_status()
+    finally:
+        _lib.set_option(_lib.OPT_PAIR, old)
+    ref = mx.gemm_mxfp4_ref(a.cpu().numpy(), b.cpu().numpy(), sa.cpu().numpy(), sb.cpu().numpy())
+    assert_close(as_f32(c), mx.bf16_bits_to_f32(ref), TOL_F8)
+
+
+@pytest.mark.parametrize("kind", ["mxfp4", "mxe5m2"])
+def test_preblocked_scales_match_per_call_relayout(cuda_device, kind):
+    """Scales converted once with block_scales give bit-identical results to
+    scales relaid on every call."""
+    M, N, K = 384, 640, 1536
+    if kind == "mxfp4":
+        a, b, sa, sb = _reference_style_mxfp4(M, N, K, 23)
+        c0 = a4w4.matmul(a, b, sa, sb)
+        c1 = a4w4.matmul(a, b, ops.block_scales(sa), ops.block_scales(sb))
+    else:
+        xa, xb, ea, eb = _mx_e5m2_inputs(M, N, K, 29)
+        qa, qb = ops.quantize_mxe5m2(xa, ea), ops.quantize_mxe5m2(xb, eb)
+        c0 = ops.gemm_f8(qa, qb, a_scales=ea, b_scales=eb, out_dtype=torch.bfloat16)
+        c1 = ops.gemm_f8(qa, qb, a_scales=ops.block_scales(ea), b_scales=eb,
+                         out_dtype=torch.bfloat16)
+    ops.check_status()
+    assert torch.equal(c0, c1)

@@ -26,7 +26,7 @@ SHAPES = [
 ]
 
 
-@pytest.fixture(params=[(0, 1), (1, 1), (2, 1), (1, 0), (2, 0)],
+@pytest.fixture(params=[(0, 1), (1, 1), (2, 1), (3, 1), (1, 0), (2, 0), (3, 0)],
                 ids=lambda p: f"sk{p[0]}-pair{p[1]}")
 def options(request):
     sk, pair = request.param
@@ -53,7 +53,7 @@ def test_schedule_covers_every_iteration_once(options, shape, num_sms):
     for u in range(p["launched"]):
         items = ops.plan_items(kind, M, N, K, u, num_sms)
         seen_sk = False
-        for idx, (t, tm, tn, kb, ke, role, first, last) in enumerate(items):
+        for idx, (t, tm, tn, kb, ke, role, first, n_c, stride) in enumerate(items):
             assert 0 <= t < tiles and 0 <= tm < p["tiles_m"] and 0 <= tn < p["tiles_n"]
             assert coords.setdefault(t, (tm, tn)) == (tm, tn)
             assert 0 <= kb < ke <= p["k_iters"]
@@ -67,7 +67,7 @@ def test_schedule_covers_every_iteration_once(options, shape, num_sms):
             if role == ROLE_OWNER:
                 assert kb == 0 and ke < p["k_iters"]
                 assert t not in owners
-                owners[t] = (u, first, last)
+                owners[t] = (u, [first + i * stride for i in range(n_c)])
                 assert idx == len(items) - 1  # the owner's wait is its last item
             if t >= p["dp_tiles"]:
                 seen_sk = True
@@ -75,9 +75,9 @@ def test_schedule_covers_every_iteration_once(options, shape, num_sms):
     assert all(v == 1 for v in cover.values())
     assert len(set(coords.values())) == tiles
     for t, units in contrib_of.items():
-        u, first, last = owners[t]
-        assert units == list(range(first, last + 1))
-        assert u < first
+        u, listed = owners[t]
+        assert sorted(units) == listed
+        assert u < min(listed)
     assert set(owners) == set(contrib_of)
 
 
@@ -85,6 +85,7 @@ def test_default_plan_for_the_headline_config():
     p = ops.plan(_lib.KIND_F16, 4096, 4096, 8192, 148)
     assert p["cta_group"] == 2 and p["units"] == 74
     assert p["tiles_m"] * p["tiles_n"] == 256
-    assert p["dp_tiles"] == 222 and p["sk_units"] == 74
+    # 3 full waves of 74 pair tiles, then 34 tiles split in 2 k-halves on 68 pairs
+    assert p["dp_tiles"] == 222 and p["splits"] == 2 and p["sk_units"] == 68
     p = ops.plan(_lib.KIND_MXFP4, 4096, 4096, 8192, 148)
-    assert p["cta_group"] == 1 and p["units"] == 148 and p["k_iters"] == 32
+    assert p["cta_group"] == 2 and p["units"] == 74 and p["k_iters"] == 32
