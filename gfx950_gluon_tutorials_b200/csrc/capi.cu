@@ -349,6 +349,13 @@ int run_gemm(const GemmCall& c) {
     if (rc != B2G_OK) return rc;
   }
   prm.partials = g.partial_bytes ? reinterpret_cast<float*>(ws + g.partial_off) : nullptr;
+  if (prm.partials != nullptr) {
+    rc = encode_2d(&prm.tmP, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, prm.partials, 256,
+                   static_cast<uint64_t>(g.plan.sk_units) * g.cg * 128, 1024, 32, 32,
+                   CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != B2G_OK) return rc;
+    prm.has_tmp = 1;
+  }
   prm.flags = g.flags_bytes ? reinterpret_cast<uint32_t*>(ws + g.flags_off) : nullptr;
   prm.status = c.status;
   prm.plan = g.plan;

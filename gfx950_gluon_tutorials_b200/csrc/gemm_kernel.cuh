@@ -55,6 +55,7 @@ struct alignas(64) GemmParams {
   CUtensorMap tmC;
   CUtensorMap tmSFA;    // blocked scales of A (u32 view: 128 words per 128-row group)
   CUtensorMap tmSFB;    // blocked scales of B
+  CUtensorMap tmP;      // split-tile partials as fp32 rows of 256 (32 x 32 boxes, 128B swizzle)
   float* partials;      // split-tile partials, one 128 x 256 fp32 slot per CTA
   uint32_t* flags;      // split-tile flags, one per (unit, CTA of pair, epilogue warp)
   int* status;          // device status word, may be null
@@ -62,6 +63,7 @@ struct alignas(64) GemmParams {
   int32_t M, N, K;
   int32_t inject;       // test hook: 1 = split-tile owners wait for a flag nobody raises
   int32_t prefetch;     // k-iterations the producer pulls into L2 ahead of its loads
+  int32_t has_tmp;      // tmP is valid
   uint64_t timeout_ns;
 };
 
@@ -109,8 +111,8 @@ struct SmemPlan {
   static constexpr uint32_t kSfbOff = kSfaOff + STAGES * kSfaBytes;
   static constexpr uint32_t kEpiOff = ((kSfbOff + STAGES * kSfbBytes) + 1023u) & ~1023u;
   static constexpr uint32_t kBarOff = kEpiOff + 4 * kEpiBufs * kEpiBufBytes;
-  // full[S], empty[S], acc_full[2], acc_empty[2], ovl, drain
-  static constexpr uint32_t kNumBars = 2 * STAGES + 6;
+  // full[S], empty[S], acc_full[2], acc_empty[2], ovl, drain, fixup[4]
+  static constexpr uint32_t kNumBars = 2 * STAGES + 10;
   static constexpr uint32_t kMiscOff = kBarOff + kNumBars * 8;  // tmem slot, abort flag
   static constexpr uint32_t kBytes = kMiscOff + 16;
   static constexpr uint32_t kDynBytes = kBytes + 1024;  // + alignment slack
@@ -218,6 +220,7 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ge
   auto acce_bar = [&](uint32_t b) { return bar0 + 8u * (2 * STAGES + 2 + b); };
   const uint32_t ovl_bar = bar0 + 8u * (2 * STAGES + 4);
   const uint32_t drain_bar = bar0 + 8u * (2 * STAGES + 5);
+  auto fix_bar = [&](uint32_t q) { return bar0 + 8u * (2 * STAGES + 6 + q); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SP::kMiscOff);
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + SP::kMiscOff + 4);
 
@@ -232,11 +235,13 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ge
     }
     mbar_init(ovl_bar, 4 * CG);
     mbar_init(drain_bar, 1);
+    for (uint32_t q = 0; q < 4; ++q) mbar_init(fix_bar(q), 1);
     *abort_flag = 0u;
     fence_mbarrier_init();
     prefetch_tensormap(&p.tmA);
     prefetch_tensormap(&p.tmB);
     prefetch_tensormap(&p.tmC);
+    if (p.has_tmp) prefetch_tensormap(&p.tmP);
     if constexpr (kScaled) {
       prefetch_tensormap(&p.tmSFA);
       prefetch_tensormap(&p.tmSFB);
@@ -424,8 +429,43 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ge
       const int32_t n0 = w.tn * 256;
       // with overlapping accumulators the shared 32 columns are drained first
       const uint32_t first_chunk = kScaled ? (b == 0 ? 7u : 0u) : 0u;
-      bool contribs_ready = w.role != kRoleOwner;
+      // A split item that is this unit's last one finds the operand ring idle
+      // (all its loads were consumed): each epilogue warp then moves its 32 x
+      // 256 fp32 partial through its own 32 KB of the ring with bulk TMA copies
+      // instead of per-thread global loads / stores.
+      const bool last_item = [&] {
+        WorkCursor c2 = cur;
+        WorkItem w2;
+        return !cursor_next(p.plan, unit, c2, w2);
+      }();
+      const bool ring_fix = last_item && w.role != kRoleFull && p.has_tmp != 0;
+      uint8_t* ring = smem + quad * 32768u;
       bool failed = false;
+      int32_t glob_first = w.first_contrib, glob_n = w.n_contrib;
+      if (w.role == kRoleOwner) {
+        bool fok = true;
+        for (int32_t ci2 = 0, u2 = w.first_contrib; ci2 < w.n_contrib && fok;
+             ++ci2, u2 += w.contrib_stride)
+          fok = wait_flag(p.flags + flag_index(u2, rank, quad, CG), p.inject ? 2u : 1u,
+                          abort_flag, p, B2G_SITE_FLAG);
+        fok = __all_sync(0xffffffffu, fok);
+        if (fok && ring_fix) {
+          fence_proxy_async_all();  // partials seen by the flag acquire -> TMA reads
+          if (lane == 0) {
+            mbar_arrive_expect_tx(fix_bar(quad), 8u * 4096u);
+            const int32_t y = (w.first_contrib * CG + static_cast<int32_t>(rank)) * 128 +
+                              static_cast<int32_t>(quad) * 32;
+            for (uint32_t c = 0; c < 8; ++c)
+              tma_load_2d(smem_u32(ring) + c * 4096u, &p.tmP, fix_bar(quad),
+                          static_cast<int32_t>(c * 32u), y);
+          }
+          fok = wait_phase<false>(fix_bar(quad), 0, abort_flag, p, B2G_SITE_FLAG);
+          fok = __all_sync(0xffffffffu, fok);
+          glob_first += w.contrib_stride;
+          glob_n -= 1;
+        }
+        if (!fok) break;
+      }
 #pragma unroll 1
       for (uint32_t ci = 0; ci < 8; ++ci) {
         const uint32_t c = (first_chunk + ci) & 7u;
@@ -445,31 +485,37 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ge
           }
         }
         if (w.role == kRoleContrib) {
-          float4* dst = reinterpret_cast<float4*>(p.partials + partial_slot(unit, rank, CG) +
-                                                  static_cast<size_t>(row) * 256u + c * 32u);
+          if (ring_fix) {
+            // 32 rows x 32 fp32 in the 128-byte swizzle, one box per chunk
+            uint8_t* box = ring + c * 4096u + lane * 128u;
 #pragma unroll
-          for (int i = 0; i < 8; ++i)
-            __stcg(dst + i, make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
-                                        __uint_as_float(v[4 * i + 2]),
-                                        __uint_as_float(v[4 * i + 3])));
+            for (uint32_t q = 0; q < 8; ++q)
+              *reinterpret_cast<uint4*>(box + ((q ^ (lane & 7u)) << 4)) =
+                  make_uint4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+          } else {
+            float4* dst = reinterpret_cast<float4*>(p.partials + partial_slot(unit, rank, CG) +
+                                                    static_cast<size_t>(row) * 256u + c * 32u);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              __stcg(dst + i,
+                     make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                                 __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3])));
+          }
           continue;
         }
         if (w.role == kRoleOwner) {
-          if (!contribs_ready) {
-            bool fok = true;
-            for (int32_t ci2 = 0, u2 = w.first_contrib; ci2 < w.n_contrib && fok;
-                 ++ci2, u2 += w.contrib_stride)
-              fok = wait_flag(p.flags + flag_index(u2, rank, quad, CG), p.inject ? 2u : 1u,
-                              abort_flag, p, B2G_SITE_FLAG);
-            fok = __all_sync(0xffffffffu, fok);
-            if (!fok) {
-              failed = true;
-              break;
+          if (ring_fix) {
+            const uint8_t* box = ring + c * 4096u + lane * 128u;
+#pragma unroll
+            for (uint32_t q = 0; q < 8; ++q) {
+              const float4 t = *reinterpret_cast<const float4*>(box + ((q ^ (lane & 7u)) << 4));
+              v[4 * q + 0] = __float_as_uint(__uint_as_float(v[4 * q + 0]) + t.x);
+              v[4 * q + 1] = __float_as_uint(__uint_as_float(v[4 * q + 1]) + t.y);
+              v[4 * q + 2] = __float_as_uint(__uint_as_float(v[4 * q + 2]) + t.z);
+              v[4 * q + 3] = __float_as_uint(__uint_as_float(v[4 * q + 3]) + t.w);
             }
-            contribs_ready = true;
           }
-          for (int32_t ci2 = 0, u2 = w.first_contrib; ci2 < w.n_contrib;
-               ++ci2, u2 += w.contrib_stride) {
+          for (int32_t ci2 = 0, u2 = glob_first; ci2 < glob_n; ++ci2, u2 += w.contrib_stride) {
             const float4* src = reinterpret_cast<const float4*>(
                 p.partials + partial_slot(u2, rank, CG) + static_cast<size_t>(row) * 256u +
                 c * 32u);
@@ -515,7 +561,21 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ge
       }
       if (failed) break;
       if (w.role == kRoleContrib) {
-        __threadfence();
+        if (ring_fix) {
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            const int32_t y = (unit * CG + static_cast<int32_t>(rank)) * 128 +
+                              static_cast<int32_t>(quad) * 32;
+            for (uint32_t c = 0; c < 8; ++c)
+              tma_store_2d(&p.tmP, smem_u32(ring + c * 4096u), static_cast<int32_t>(c * 32u), y);
+            bulk_commit_group();
+            bulk_wait_group<0>();   // partial written to global memory
+            fence_proxy_async_all();
+          }
+        } else {
+          __threadfence();
+        }
         __syncwarp();
         if (lane == 0) st_release_gpu(p.flags + flag_index(unit, rank, quad, CG), 1u);
       } else if (w.role == kRoleOwner) {
