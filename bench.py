@@ -30,7 +30,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -66,63 +65,78 @@ def tensor_peak(dtype_name: str, peaks: dict) -> float:
 
 
 class ClockSampler:
-    """nvidia-smi samples of SM clock and throttle reasons while timing."""
+    """SM clock and throttle reasons sampled while timing.
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    Polls NVML from a background thread every ~2 ms (the timed region of a
+    default run is only tens of ms); falls back to `nvidia-smi -lms` when the
+    NVML bindings are missing."""
+
+    REASONS = {  # NVML clocks-event reason bits reported as rejection criteria
+        "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+        "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80,
+    }
 
     def __init__(self, index: int):
         self.index = index
-        self.proc = None
-        self.lines: list[str] = []
+        self.samples: list[tuple[float, float, int, float]] = []
+        self._stop = threading.Event()
         self.thread = None
+        self.nvml = None
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
-                 "--format=csv,noheader,nounits", "-lms", "20"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.handle = pynvml.nvmlDeviceGetHandleByIndex(self._physical_index())
+        except Exception:  # noqa: BLE001 - no NVML: report the absence
+            self.nvml = None
             return
-        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread = threading.Thread(target=self._poll, daemon=True)
         self.thread.start()
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def _physical_index(self) -> int:
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        if vis:
+            try:
+                return int(vis.split(",")[self.index])
+            except (ValueError, IndexError):
+                pass
+        return self.index
 
-    def stop(self) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
+    def _poll(self):
+        n = self.nvml
+        while not self._stop.is_set():
+            try:
+                sm = n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM)
+                smax = n.nvmlDeviceGetMaxClockInfo(self.handle, n.NVML_CLOCK_SM)
+                reasons = n.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                power = n.nvmlDeviceGetPowerUsage(self.handle) / 1000.0
+                self.samples.append((float(sm), float(smax), int(reasons), power,
+                                     time.perf_counter()))
+            except Exception:  # noqa: BLE001
+                break
+            time.sleep(0.002)
+
+    def stop(self, window: tuple[float, float] | None = None) -> dict:
+        """Summary of the samples taken inside `window` (host perf_counter times
+        bracketing the timed region), or of all samples if none fall inside."""
+        if self.nvml is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"]}
+        self._stop.set()
         if self.thread is not None:
             self.thread.join(timeout=2)
-        sm, smax, reasons, power = [], [], set(), []
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                smax.append(float(parts[2]))
-                power.append(float(parts[3]))
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(smax) if smax else None,
-                "power_w_max": max(power) if power else None,
-                "samples": len(sm), "reasons": sorted(reasons)}
+        sel = self.samples
+        if window is not None:
+            inside = [x for x in self.samples if window[0] <= x[4] <= window[1]]
+            sel = inside or self.samples
+        if not sel:
+            return {"sm_mhz": None, "sm_max_mhz": None, "samples": 0, "reasons": []}
+        sm = [x[0] for x in sel]
+        reasons = sorted({name for x in sel for name, bit in self.REASONS.items() if x[2] & bit})
+        return {"sm_mhz": statistics.median(sm), "sm_min_mhz": min(sm),
+                "sm_max_mhz": max(x[1] for x in sel), "power_w_max": max(x[3] for x in sel),
+                "samples": len(sel), "reasons": reasons}
 
 
 def dist_setup(n_gpus: int):
@@ -217,19 +231,25 @@ class Workload:
         return sum(t.numel() * t.element_size() for t in s.values())
 
 
-def time_device(w: Workload, steps: int, warmup: int, world: int) -> float:
-    """ms per step: CUDA events on the launching stream, max over ranks."""
+def time_device(w: Workload, steps: int, warmup: int, world: int, marks: list | None = None
+                ) -> float:
+    """ms per step: CUDA events on the launching stream, max over ranks. `marks`
+    receives the host times bracketing the timed region."""
     for i in range(warmup):
         w.run(i)
     barrier(world)
     stream = torch.cuda.current_stream()
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
     start.record(stream)
     for i in range(steps):
         w.run(warmup + i)
     end.record(stream)
     torch.cuda.synchronize()
+    t1 = time.perf_counter()
+    if marks is not None:
+        marks.extend([t0, t1])
     ms = start.elapsed_time(end) / steps
     barrier(world)
     w.ops.check_status()
@@ -343,8 +363,9 @@ def contract_main(args):
         nsets = 2
     w = Workload("head", M, n_local, K, head_name, sets=nsets, seed=1234 + rank)
     clocks.start()
-    ms = time_device(w, args.steps, args.warmup, world)
-    clock_info = clocks.stop()
+    marks: list = []
+    ms = time_device(w, args.steps, args.warmup, world, marks)
+    clock_info = clocks.stop((marks[0], marks[1]))
     flops_total = w.flops * world
     value = flops_total / (ms * 1e-3) / 1e12
     per_gpu = value / world
