@@ -305,16 +305,16 @@ def time_allgather(w: Workload, world: int, iters: int = 10) -> dict | None:
     [world][M][N/world] buffer in each GPU's own memory."""
     if world == 1:
         return None
+    from gfx950_gluon_tutorials_b200.shard import gather_slabs
     c = w.sets[0]["c"]
-    out = torch.empty((world,) + tuple(c.shape), dtype=c.dtype, device=c.device)
     for _ in range(3):
-        torch.distributed.all_gather_into_tensor(out, c)
+        out = gather_slabs(c)
     barrier(world)
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     start.record()
     for _ in range(iters):
-        torch.distributed.all_gather_into_tensor(out, c)
+        out = gather_slabs(c)
     end.record()
     torch.cuda.synchronize()
     ms = max_over_ranks(start.elapsed_time(end) / iters, world)
