@@ -23,6 +23,7 @@ STATUS_TIMEOUT = 0x1000
 SITE_EMPTY, SITE_FULL, SITE_ACC_EMPTY, SITE_ACC_FULL, SITE_OVERLAP, SITE_FLAG = 1, 2, 3, 4, 5, 6
 OPT_PAIR, OPT_SK_MODE, OPT_GROUP_M, OPT_MIN_SK_ITERS, OPT_TIMEOUT_MS = 1, 2, 3, 4, 5
 OPT_INJECT_FLAG_TIMEOUT, OPT_MAX_UNITS, OPT_L2_PREFETCH = 6, 7, 8
+NOALLOC_SCRATCH_BYTES = 32 << 20
 
 _c_int, _c_i64, _c_sz, _vp = ctypes.c_int, ctypes.c_int64, ctypes.c_size_t, ctypes.c_void_p
 _i32p = ctypes.POINTER(ctypes.c_int32)
@@ -40,6 +41,9 @@ SIGNATURES = {
     "b2g_gemm_mxf4": (_c_int, [_vp, _c_i64, _vp, _c_i64, _vp, _c_i64, _c_i64, _vp, _c_i64,
                                _c_i64, _vp, _c_i64, _c_int, _c_int, _c_int, _c_int, _vp, _c_sz,
                                _vp, _vp]),
+    "b2g_gemm_mxf4_noalloc": (_c_int, [_vp, _c_i64, _vp, _c_i64, _vp, _c_i64, _c_i64, _vp,
+                                       _c_i64, _c_i64, _vp, _c_i64, _c_int, _c_int, _c_int,
+                                       _c_int, _vp, _vp]),
     "b2g_quant_mxfp4": (_c_int, [_vp, _c_i64, _c_int, _c_int, _vp, _c_i64, _vp, _c_i64, _c_i64,
                                  _vp]),
     "b2g_quant_mxe5m2": (_c_int, [_vp, _c_i64, _c_int, _c_int, _vp, _c_i64, _c_i64, _vp, _c_i64,

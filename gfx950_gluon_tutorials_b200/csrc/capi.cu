@@ -11,6 +11,7 @@
 #include <mutex>
 
 #include "b2g.h"
+#include "capi_internal.h"
 #include "gemm_kernel.cuh"
 #include "pack.cuh"
 #include "sched.h"
@@ -369,6 +370,41 @@ int run_gemm(const GemmCall& c) {
 }
 
 }  // namespace
+
+namespace b2g {
+
+int gemm_mxf4_fixed_scratch(const uint8_t* A, int64_t lda, const uint8_t* B, int64_t ldb,
+                            const uint8_t* sfa, int64_t sfa_s0, int64_t sfa_s1,
+                            const uint8_t* sfb, int64_t sfb_s0, int64_t sfb_s1, void* C,
+                            int64_t ldc, int M, int N, int K, int out_dtype, void* scratch,
+                            size_t capacity, int* status, cudaStream_t stream) {
+  GemmCall c{};
+  c.kind = B2G_KIND_MXFP4;
+  c.A = A; c.lda = lda; c.B = B; c.ldb = ldb;
+  c.sfa = sfa; c.sfa_s0 = sfa_s0; c.sfa_s1 = sfa_s1;
+  c.sfb = sfb; c.sfb_s0 = sfb_s0; c.sfb_s1 = sfb_s1;
+  c.C = C; c.ldc = ldc; c.M = M; c.N = N; c.K = K; c.out_dtype = out_dtype;
+  c.ws = scratch; c.ws_bytes = capacity; c.status = status;
+  c.stream = stream;
+  int rc = check_call(c);
+  if (rc != B2G_OK) return rc;
+  int dev = -1;
+  cudaGetDevice(&dev);
+  const int sms = current_sms();
+  if (sms <= 0) return B2G_ENODEVICE;
+  const Geometry g = geometry(c.kind, c.M, c.N, c.K, sms, pair_capacity(dev, sms));
+  if (g.total > capacity) return B2G_ECAPACITY;
+  if (g.flags_bytes > 0) {
+    // the scratch is not the caller's to reset, so a call that timed out must
+    // not leave flags behind for the next one: clear them in stream order
+    const cudaError_t e =
+        cudaMemsetAsync(static_cast<uint8_t*>(scratch) + g.flags_off, 0, g.flags_bytes, stream);
+    if (e != cudaSuccess) return static_cast<int>(e);
+  }
+  return run_gemm(c);
+}
+
+}  // namespace b2g
 
 extern "C" {
 

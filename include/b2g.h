@@ -125,6 +125,37 @@ B2G_API int b2g_gemm_mxf4(const uint8_t* A, int64_t lda, const uint8_t* B, int64
                   int out_dtype, void* workspace, size_t workspace_bytes, int* status,
                   void* stream);
 
+/* a4w4 without a workspace. This entry point has no counterpart in the
+ * reference (whose launchers always let torch allocate); it serves callers
+ * that cannot allocate device memory per call: a process that reserves HBM
+ * for its own pool up front, or an FFI host with no caching allocator, for
+ * which cudaMalloc / cudaFree around each call would fail or stall the device.
+ * It computes what b2g_gemm_mxf4 computes, with the same arguments minus the
+ * workspace, and allocates nothing: its scratch (stream-K flag words, split
+ * partial sums, relaid scales) is a static device array of
+ * B2G_NOALLOC_SCRATCH_BYTES inside the library, one copy per device.
+ * - Limit: a call needs b2g_gemm_workspace_bytes(B2G_KIND_MXFP4, M, N, K)
+ *   bytes (4096 x 4096 x 8192 needs about 19 MiB on a 148-SM B200); above
+ *   the capacity it returns B2G_ECAPACITY and launches nothing.
+ * - Zero state: the flag words must be zero when a GEMM launch starts. The
+ *   array is zero when the library's module is loaded on a device, and each
+ *   call also clears its flag words on `stream` (a memset, no allocation)
+ *   before the launch; partial sums and relaid scales need no initial value.
+ * - Set-up: the first call on each device, made while that device is
+ *   current, looks up the scratch address (cudaGetSymbolAddress, which may
+ *   load the module onto the device) together with the set-up every entry
+ *   point does once per device. Make that first call before any stream
+ *   capture begins.
+ * - Races: one scratch per device means calls on the same device must not
+ *   overlap on the GPU (use one stream, or order streams with events);
+ *   overlapping calls corrupt each other's flags and partial sums. */
+#define B2G_NOALLOC_SCRATCH_BYTES 33554432 /* 32 MiB per device */
+B2G_API int b2g_gemm_mxf4_noalloc(const uint8_t* A, int64_t lda, const uint8_t* B, int64_t ldb,
+                                  const uint8_t* sfa, int64_t sfa_s0, int64_t sfa_s1,
+                                  const uint8_t* sfb, int64_t sfb_s0, int64_t sfb_s1, void* C,
+                                  int64_t ldc, int M, int N, int K, int out_dtype, int* status,
+                                  void* stream);
+
 /* Blocked E8M0 scale layout: for each 128-row block and each group of 4
  * k-blocks (4 scales), 512 bytes in which byte r0*16 + r1*4 + j holds the
  * scale of row 128*block + 32*r1 + r0 for k-block 4*group + j; blocks are
