@@ -18,6 +18,18 @@
 
 using namespace b2g;
 
+// Ring depths (stages of 128 bytes of K) per CTA shape; the shared-memory
+// plan must fit 227 KB (checked at compile time).
+#ifndef B2G_STAGES_CG1
+#define B2G_STAGES_CG1 4
+#endif
+#ifndef B2G_STAGES_CG2
+#define B2G_STAGES_CG2 6
+#endif
+#ifndef B2G_STAGES_CG2_SCALED
+#define B2G_STAGES_CG2_SCALED 5
+#endif
+
 namespace {
 
 // ------------------------------------------------------------- options --
@@ -63,7 +75,7 @@ int pair_capacity(int dev, int sms) {
   if (dev < 0 || dev >= kMaxDevices) return sms / 2;
   int v = cache[dev].load();
   if (v > 0) return v;
-  constexpr int kStages = 6;
+  constexpr int kStages = B2G_STAGES_CG2;
   using SP = SmemPlan<kKindF16, 2, kStages>;
   auto kern = gemm_kernel<kKindF16, 2, kStages, false>;
   int n = 0;
@@ -188,9 +200,9 @@ int encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t
 template <int KIND, int CG, bool OB>
 int launch_gemm_t(const GemmParams& prm, int units, cudaStream_t stream) {
   constexpr bool kScaled = KindTraits<KIND>::kScaled;
-  constexpr int kStages = CG == 1 ? 4 : (kScaled ? 5 : 6);
+  constexpr int kStages = CG == 1 ? B2G_STAGES_CG1 : (kScaled ? B2G_STAGES_CG2_SCALED : B2G_STAGES_CG2);
   using SP = SmemPlan<KIND, CG, kStages>;
-  static_assert(SP::kDynBytes <= 232448, "shared memory plan exceeds 227 KB");
+  static_assert(SP::kDynBytes <= SP::kMaxDyn, "shared memory plan exceeds 227 KB");
   auto kern = gemm_kernel<KIND, CG, kStages, OB>;
   static std::atomic<uint64_t> attr_done{0};  // bit per device
   int dev = 0;
@@ -432,6 +444,9 @@ const char* b2g_strerror(int code) {
     case B2G_ETENSORMAP: return "TMA descriptor rejected by the driver";
     case B2G_ENODEVICE: return "no sm_100 device is current";
     case B2G_ECAPACITY: return "size exceeds the entry point's fixed capacity";
+    case B2G_STATUS_SMEM_BASE:
+      return "kernel refused to run: dynamic shared memory base needs more alignment padding "
+             "than was reserved";
     default: break;
   }
   if (code > 0) return cudaGetErrorString(static_cast<cudaError_t>(code));

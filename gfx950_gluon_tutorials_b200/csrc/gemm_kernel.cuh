@@ -115,7 +115,14 @@ struct SmemPlan {
   static constexpr uint32_t kNumBars = 2 * STAGES + 10;
   static constexpr uint32_t kMiscOff = kBarOff + kNumBars * 8;  // tmem slot, abort flag
   static constexpr uint32_t kBytes = kMiscOff + 16;
-  static constexpr uint32_t kDynBytes = kBytes + 1024;  // + alignment slack
+  // The carve-up starts on a 1024-byte boundary (128-byte-swizzled TMA tiles).
+  // Up to 1 KB of slack is reserved for rounding the dynamic base up to it;
+  // plans that fill the 227 KB limit reserve what is left, and the kernel
+  // refuses to run if its base would need more.
+  static constexpr uint32_t kMaxDyn = 232448;
+  static constexpr uint32_t kSlack =
+      kBytes + 1024 <= kMaxDyn ? 1024u : (kBytes <= kMaxDyn ? (kMaxDyn - kBytes) & ~15u : 0u);
+  static constexpr uint32_t kDynBytes = kBytes + kSlack;
 
   // bytes the TMA lands per stage on the leader's full barrier (both CTAs)
   static constexpr uint32_t kTxBytes = CG * (kABytes + kBBytes + kSfaBytes + kSfbBytes);
@@ -153,6 +160,18 @@ __device__ __noinline__ bool wait_phase(uint32_t bar, uint32_t parity, volatile 
       return false;
     }
   }
+}
+
+// wait_phase behind an inlined single probe. The ring's full barriers complete
+// through TMA transaction bytes and are read only by tcgen05 operations, so
+// the per-stage probe needs no cluster-scope acquire; a miss falls back to the
+// bounded wait (with `kClusterScope` probes).
+template <bool kClusterScope>
+__device__ __forceinline__ bool wait_phase_fast(uint32_t bar, uint32_t parity,
+                                                volatile uint32_t* abort_flag,
+                                                const GemmParams& p, int site) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return wait_phase<kClusterScope>(bar, parity, abort_flag, p, site);
 }
 
 // Bounded wait for a global split-tile flag to reach `want`.
@@ -206,6 +225,11 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ge
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
+  if (static_cast<uint32_t>(smem - smem_raw) > SP::kSlack) {
+    // the same for every CTA of the launch: nothing has been touched yet
+    if (threadIdx.x == 0) report_status(p, B2G_STATUS_SMEM_BASE);
+    return;
+  }
   const uint32_t sbase = smem_u32(smem);
   const uint32_t warp = threadIdx.x >> 5;
   const uint32_t lane = threadIdx.x & 31;
@@ -290,7 +314,7 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ge
         for (int32_t k = w.k_begin; k < w.k_end; ++k, ++it) {
           const uint32_t s = it % STAGES, ph = (it / STAGES) & 1u;
           if (p.prefetch > 0) prefetch_one();
-          if (!wait_phase<false>(empty_bar(s), ph ^ 1u, abort_flag, p, B2G_SITE_EMPTY)) {
+          if (!wait_phase_fast<false>(empty_bar(s), ph ^ 1u, abort_flag, p, B2G_SITE_EMPTY)) {
             alive = false;
             break;
           }
@@ -350,7 +374,7 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ge
         const uint32_t d_tmem = tmem_base + b * SP::kAccStride;
         for (int32_t k = w.k_begin; k < w.k_end; ++k, ++it) {
           const uint32_t s = it % STAGES, ph = (it / STAGES) & 1u;
-          if (!wait_phase<CG == 2>(full_bar(s), ph, abort_flag, p, B2G_SITE_FULL)) {
+          if (!wait_phase_fast<false>(full_bar(s), ph, abort_flag, p, B2G_SITE_FULL)) {
             alive = false;
             break;
           }
