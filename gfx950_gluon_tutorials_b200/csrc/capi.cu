@@ -18,16 +18,16 @@
 
 using namespace b2g;
 
-// Ring depths (stages of 128 bytes of K) per CTA shape; the shared-memory
+// Ring depths (stages of kKChunks x 128 bytes of K) per CTA shape; the shared-memory
 // plan must fit 227 KB (checked at compile time).
 #ifndef B2G_STAGES_CG1
-#define B2G_STAGES_CG1 4
+#define B2G_STAGES_CG1 2
 #endif
 #ifndef B2G_STAGES_CG2
-#define B2G_STAGES_CG2 6
+#define B2G_STAGES_CG2 3
 #endif
 #ifndef B2G_STAGES_CG2_SCALED
-#define B2G_STAGES_CG2_SCALED 5
+#define B2G_STAGES_CG2_SCALED 3
 #endif
 
 namespace {
@@ -153,7 +153,8 @@ Geometry geometry(int kind, int M, int N, int K, int sms, int pair_cap = 0) {
   if (units < 1) units = 1;
   const int tiles_m = (M + 128 * g.cg - 1) / (128 * g.cg);
   const int tiles_n = (N + 255) / 256;
-  const int k_iters = static_cast<int>((row_bytes(kind, K) + 127) / 128);
+  const int k_chunks = static_cast<int>((row_bytes(kind, K) + 127) / 128);
+  const int k_iters = (k_chunks + kKChunks - 1) / kKChunks;
   g.plan = make_plan(tiles_m, tiles_n, k_iters, units, static_cast<int>(g_opt.group_m.load()),
                      static_cast<int>(g_opt.sk_mode.load()),
                      static_cast<int>(g_opt.min_sk_iters.load()));
@@ -378,6 +379,7 @@ int run_gemm(const GemmCall& c) {
   prm.inject = static_cast<int32_t>(g_opt.inject.load());
   prm.prefetch = static_cast<int32_t>(g_opt.prefetch.load());
   prm.timeout_ns = static_cast<uint64_t>(g_opt.timeout_ms.load()) * 1000000ull;
+  prm.k_chunks = static_cast<int32_t>((rb + 127) / 128);
   return dispatch(c.kind, g.cg, prm, g.launched, c.out_dtype, c.stream);
 }
 

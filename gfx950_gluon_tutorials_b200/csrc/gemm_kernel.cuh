@@ -24,8 +24,11 @@
 // rows (two 512-byte blocks per group), which the pair's tcgen05.cp copies
 // into each CTA's TMEM.
 //
-// Every K stage moves 128 bytes of K per row: 64 fp16/bf16, 128 e5m2 or 256
-// packed e2m1 elements, i.e. four MMAs of 32 bytes of K each.
+// Every K stage moves kKChunks chunks of 128 bytes of K per row (one TMA box
+// per operand and chunk): a chunk is 64 fp16/bf16, 128 e5m2 or 256 packed
+// e2m1 elements, i.e. four MMAs of 32 bytes of K. Two chunks per stage halve
+// the per-K cost of the MMA thread's barrier wait, commit and loop control,
+// which otherwise outlast the MMAs themselves.
 //
 // All waits are bounded (iteration probes plus a %globaltimer deadline). On a
 // timeout the CTA records a status code, raises a CTA-wide abort flag, drains
@@ -40,6 +43,9 @@
 #include "sched.h"
 
 namespace b2g {
+
+// 128-byte K chunks per pipeline stage (k-iterations count stages).
+constexpr int kKChunks = 2;
 
 enum : int {
   kKindF16 = 0,
@@ -64,6 +70,7 @@ struct alignas(64) GemmParams {
   int32_t inject;       // test hook: 1 = split-tile owners wait for a flag nobody raises
   int32_t prefetch;     // k-iterations the producer pulls into L2 ahead of its loads
   int32_t has_tmp;      // tmP is valid
+  int32_t k_chunks;     // 128-byte K chunks per row (the last stage may hold fewer)
   uint64_t timeout_ns;
 };
 
@@ -96,12 +103,18 @@ struct SmemPlan {
   static constexpr bool kScaled = KindTraits<KIND>::kScaled;
   static constexpr int kGps = KindTraits<KIND>::kGroupsPerStage;
   static constexpr uint32_t kThreads = 192;
-  static constexpr uint32_t kABytes = 128 * 128;
+  // per 128-byte K chunk
+  static constexpr uint32_t kChunkA = 128 * 128;
   static constexpr uint32_t kBRows = CG == 1 ? 256 : 128;
-  static constexpr uint32_t kBBytes = kBRows * 128;
+  static constexpr uint32_t kChunkB = kBRows * 128;
   // scales for this CTA's 128 A rows and all 256 B rows of the tile
-  static constexpr uint32_t kSfaBytes = kScaled ? kGps * 512 : 0;
-  static constexpr uint32_t kSfbBytes = kScaled ? 2 * kGps * 512 : 0;
+  static constexpr uint32_t kChunkSfa = kScaled ? kGps * 512 : 0;
+  static constexpr uint32_t kChunkSfb = kScaled ? 2 * kGps * 512 : 0;
+  // per stage
+  static constexpr uint32_t kABytes = kKChunks * kChunkA;
+  static constexpr uint32_t kBBytes = kKChunks * kChunkB;
+  static constexpr uint32_t kSfaBytes = kKChunks * kChunkSfa;
+  static constexpr uint32_t kSfbBytes = kKChunks * kChunkSfb;
   static constexpr uint32_t kEpiBufs = 2;
   static constexpr uint32_t kEpiBufBytes = 32 * 64;  // 32 rows x 32 cols x 2 B
 
@@ -124,8 +137,8 @@ struct SmemPlan {
       kBytes + 1024 <= kMaxDyn ? 1024u : (kBytes <= kMaxDyn ? (kMaxDyn - kBytes) & ~15u : 0u);
   static constexpr uint32_t kDynBytes = kBytes + kSlack;
 
-  // bytes the TMA lands per stage on the leader's full barrier (both CTAs)
-  static constexpr uint32_t kTxBytes = CG * (kABytes + kBBytes + kSfaBytes + kSfbBytes);
+  // bytes the TMA lands per chunk on the leader's full barrier (both CTAs)
+  static constexpr uint32_t kChunkTx = CG * (kChunkA + kChunkB + kChunkSfa + kChunkSfb);
 
   // TMEM columns: two accumulators (overlapping by 32 columns when scale
   // factors need room) and the scale-factor slots.
@@ -143,16 +156,18 @@ __device__ __forceinline__ void report_status(const GemmParams& p, int code) {
 template <bool kClusterScope>
 __device__ __noinline__ bool wait_phase(uint32_t bar, uint32_t parity, volatile uint32_t* abort_flag,
                                         const GemmParams& p, int site) {
+  // each probe may sleep up to 20 us; the deadline and the abort flag are
+  // checked between probes
+  constexpr uint32_t kHintNs = 20000;
   auto probe = [&]() {
-    return kClusterScope ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity);
+    return kClusterScope ? mbar_try_wait_cluster_sleep(bar, parity, kHintNs)
+                         : mbar_try_wait_sleep(bar, parity, kHintNs);
   };
   if (probe()) return true;
   const uint64_t t0 = globaltimer_ns();
 #pragma unroll 1
   while (true) {
-#pragma unroll 1
-    for (int i = 0; i < 16; ++i)
-      if (probe()) return true;
+    if (probe()) return true;
     if (*abort_flag != 0u) return false;
     if (globaltimer_ns() - t0 > p.timeout_ns) {
       report_status(p, B2G_STATUS_TIMEOUT | site);
@@ -303,8 +318,10 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ge
         if (!pf_live) return;
         const int32_t ar = pf_w.tm * (128 * CG) + static_cast<int32_t>(rank) * 128;
         const int32_t br = pf_w.tn * 256 + (CG == 2 ? static_cast<int32_t>(rank) * 128 : 0);
-        tma_prefetch_l2_2d(&p.tmA, pf_k * 128, ar);
-        tma_prefetch_l2_2d(&p.tmB, pf_k * 128, br);
+        for (int32_t c = 0; c < kKChunks && pf_k * kKChunks + c < p.k_chunks; ++c) {
+          tma_prefetch_l2_2d(&p.tmA, (pf_k * kKChunks + c) * 128, ar);
+          tma_prefetch_l2_2d(&p.tmB, (pf_k * kKChunks + c) * 128, br);
+        }
         ++pf_k;
       };
       for (int32_t i = 0; i < p.prefetch; ++i) prefetch_one();
@@ -318,29 +335,33 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ge
             alive = false;
             break;
           }
-          if (leader) mbar_arrive_expect_tx(full_bar(s), SP::kTxBytes);
+          // chunks past the end of K are neither loaded nor multiplied
+          const int32_t nc = min(kKChunks, p.k_chunks - k * kKChunks);
+          if (leader) mbar_arrive_expect_tx(full_bar(s), static_cast<uint32_t>(nc) * SP::kChunkTx);
           const uint32_t fb = CG == 1 ? full_bar(s) : map_to_cta(full_bar(s), 0);
-          const int32_t kx = k * 128;
-          const uint32_t a_dst = sbase + SP::kAOff + s * SP::kABytes;
-          const uint32_t b_dst = sbase + SP::kBOff + s * SP::kBBytes;
-          if constexpr (CG == 1) {
-            tma_load_2d(a_dst, &p.tmA, fb, kx, a_row);
-            tma_load_2d(b_dst, &p.tmB, fb, kx, b_row);
-          } else {
-            tma_load_2d_pair(a_dst, &p.tmA, fb, kx, a_row);
-            tma_load_2d_pair(b_dst, &p.tmB, fb, kx, b_row);
-          }
-          if constexpr (kScaled) {
-            // blocked scales: this CTA's 128-row group of A, both groups of the B tile
-            const uint32_t sfa_dst = sbase + SP::kSfaOff + s * SP::kSfaBytes;
-            const uint32_t sfb_dst = sbase + SP::kSfbOff + s * SP::kSfbBytes;
-            const int32_t sx = k * kGps * 128;
+          for (int32_t c = 0; c < nc; ++c) {
+            const int32_t kc = k * kKChunks + c;
+            const uint32_t a_dst = sbase + SP::kAOff + s * SP::kABytes + c * SP::kChunkA;
+            const uint32_t b_dst = sbase + SP::kBOff + s * SP::kBBytes + c * SP::kChunkB;
             if constexpr (CG == 1) {
-              tma_load_2d(sfa_dst, &p.tmSFA, fb, sx, a_row >> 7);
-              tma_load_2d(sfb_dst, &p.tmSFB, fb, sx, w.tn * 2);
+              tma_load_2d(a_dst, &p.tmA, fb, kc * 128, a_row);
+              tma_load_2d(b_dst, &p.tmB, fb, kc * 128, b_row);
             } else {
-              tma_load_2d_pair(sfa_dst, &p.tmSFA, fb, sx, a_row >> 7);
-              tma_load_2d_pair(sfb_dst, &p.tmSFB, fb, sx, w.tn * 2);
+              tma_load_2d_pair(a_dst, &p.tmA, fb, kc * 128, a_row);
+              tma_load_2d_pair(b_dst, &p.tmB, fb, kc * 128, b_row);
+            }
+            if constexpr (kScaled) {
+              // blocked scales: this CTA's 128-row group of A, both groups of the B tile
+              const uint32_t sfa_dst = sbase + SP::kSfaOff + s * SP::kSfaBytes + c * SP::kChunkSfa;
+              const uint32_t sfb_dst = sbase + SP::kSfbOff + s * SP::kSfbBytes + c * SP::kChunkSfb;
+              const int32_t sx = kc * kGps * 128;
+              if constexpr (CG == 1) {
+                tma_load_2d(sfa_dst, &p.tmSFA, fb, sx, a_row >> 7);
+                tma_load_2d(sfb_dst, &p.tmSFB, fb, sx, w.tn * 2);
+              } else {
+                tma_load_2d_pair(sfa_dst, &p.tmSFA, fb, sx, a_row >> 7);
+                tma_load_2d_pair(sfb_dst, &p.tmSFB, fb, sx, w.tn * 2);
+              }
             }
           }
         }
@@ -379,14 +400,18 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ge
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = sbase + SP::kAOff + s * SP::kABytes;
-          const uint32_t b_addr = sbase + SP::kBOff + s * SP::kBBytes;
+          const int32_t nc = min(kKChunks, p.k_chunks - k * kKChunks);
+#pragma unroll
+          for (int32_t c = 0; c < kKChunks; ++c) {
+          if (c >= nc) break;
+          const uint32_t a_addr = sbase + SP::kAOff + s * SP::kABytes + c * SP::kChunkA;
+          const uint32_t b_addr = sbase + SP::kBOff + s * SP::kBBytes + c * SP::kChunkB;
           const uint64_t adesc = sdesc_kmajor_sw128(a_addr);
           const uint64_t bdesc = sdesc_kmajor_sw128(b_addr);
           if constexpr (kScaled) {
-            // scale factors of this stage: smem -> TMEM (in issue order with the MMAs)
-            const uint32_t sfa_addr = sbase + SP::kSfaOff + s * SP::kSfaBytes;
-            const uint32_t sfb_addr = sbase + SP::kSfbOff + s * SP::kSfbBytes;
+            // scale factors of this chunk: smem -> TMEM (in issue order with the MMAs)
+            const uint32_t sfa_addr = sbase + SP::kSfaOff + s * SP::kSfaBytes + c * SP::kChunkSfa;
+            const uint32_t sfb_addr = sbase + SP::kSfbOff + s * SP::kSfbBytes + c * SP::kChunkSfb;
 #pragma unroll
             for (int g = 0; g < kGps; ++g) {
               tmem_cp_32x128b_x4<CG>(tmem_base + SP::kSfaCol + 4 * g,
@@ -402,7 +427,7 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ge
             // +32 bytes of K per MMA inside the 128-byte swizzled row
             const uint64_t ad = adesc + 2u * j;
             const uint64_t bd = bdesc + 2u * j;
-            const uint32_t acc = (k > w.k_begin || j > 0) ? 1u : 0u;
+            const uint32_t acc = (k > w.k_begin || c > 0 || j > 0) ? 1u : 0u;
             if constexpr (KIND == kKindF16 || KIND == kKindBF16) {
               mma_f16<CG>(d_tmem, ad, bd, make_idesc<KIND, CG>(0), acc);
             } else if constexpr (KIND == kKindE5M2) {
@@ -417,6 +442,7 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ge
               else
                 mma_mxf8f6f4<CG>(d_tmem, ad, bd, make_idesc<KIND, CG>(sf_id), sfa_t, sfb_t, acc);
             }
+          }
           }
           if constexpr (CG == 1)
             tc_commit<1>(empty_bar(s));

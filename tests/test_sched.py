@@ -88,4 +88,5 @@ def test_default_plan_for_the_headline_config():
     # 3 full waves of 74 pair tiles, then 34 tiles split in 2 k-halves on 68 pairs
     assert p["dp_tiles"] == 222 and p["splits"] == 2 and p["sk_units"] == 68
     p = ops.plan(_lib.KIND_MXFP4, 4096, 4096, 8192, 148)
-    assert p["cta_group"] == 2 and p["units"] == 74 and p["k_iters"] == 32
+    # 4096 bytes of packed K per row, in stages of two 128-byte chunks
+    assert p["cta_group"] == 2 and p["units"] == 74 and p["k_iters"] == 16
