@@ -433,6 +433,7 @@ const char* b2g_strerror(int code) {
       case B2G_SITE_ACC_FULL: return "timeout: epilogue waiting for an accumulator";
       case B2G_SITE_OVERLAP: return "timeout: MMA waiting for shared accumulator columns";
       case B2G_SITE_FLAG: return "timeout: stream-K owner waiting for a contributor";
+      case B2G_SITE_SCALES: return "timeout: MMA waiting for scale factors in TMEM";
       default: return "timeout in a bounded wait";
     }
   }

@@ -6,16 +6,20 @@
 //   a4w4    kernels/gemm/intra_wave/a4w4/v1_sliceMN/matmul_kernel.py:15-694
 // with one template: A is M x K and B is N x K, both K-contiguous; C is M x N.
 //
-// CTA layout (192 threads):
+// CTA layout (192 threads, 224 for MXFP4):
 //   warp 0      TMA producer: one thread fills a STAGES-deep shared-memory ring
 //               (A tile, B tile and, for block-scaled kinds, the E8M0 scales,
 //               pre-arranged in 512-byte blocks by a relayout pass).
 //   warp 1      MMA issuer: allocates all 512 TMEM columns, one thread issues
-//               tcgen05.mma into a double-buffered TMEM accumulator and copies
-//               scale factors smem -> TMEM with tcgen05.cp.
+//               tcgen05.mma into a double-buffered TMEM accumulator.
 //   warps 2-5   epilogue: TMEM -> registers -> (split-tile fixup) -> bf16/fp16
 //               -> swizzled smem -> TMA store. Warp w reads TMEM lanes
 //               32*(w%4) .. 32*(w%4)+31.
+//   warp 6      (MXFP4) scale copier: one thread copies each stage's scale
+//               factors smem -> TMEM with tcgen05.cp into one of two TMEM
+//               slots, so the MMA thread's issue slots go to MMAs. For scaled
+//               e5m2 (half the scale bytes per stage) the MMA thread issues
+//               the copies itself into a single slot, which measured faster.
 //
 // Tiles: cta_group::1 -> 128 x 256 per CTA; cta_group::2 -> 256 x 256 per CTA
 // pair, each CTA loading its own 128 rows of A and its own 128 rows of B (the
@@ -77,6 +81,9 @@ struct alignas(64) GemmParams {
 template <int KIND>
 struct KindTraits {
   static constexpr bool kScaled = KIND == kKindMXE5M2 || KIND == kKindMXFP4;
+  // scale factors copied by a dedicated warp into two TMEM slots (else by the
+  // MMA thread, in issue order with the MMAs, into one slot)
+  static constexpr bool kSfWarp = KIND == kKindMXFP4;
   // 4-scale groups (one 512-byte atom per 128 rows) per stage: a stage holds
   // 128 bytes of K per row = 128 e5m2 (4 scales) or 256 e2m1 (8 scales).
   static constexpr int kGroupsPerStage = KIND == kKindMXFP4 ? 2 : 1;
@@ -102,7 +109,9 @@ template <int KIND, int CG, int STAGES>
 struct SmemPlan {
   static constexpr bool kScaled = KindTraits<KIND>::kScaled;
   static constexpr int kGps = KindTraits<KIND>::kGroupsPerStage;
-  static constexpr uint32_t kThreads = 192;
+  static constexpr bool kSfWarp = KindTraits<KIND>::kSfWarp;
+  static constexpr uint32_t kSfSlots = kSfWarp ? 2 : 1;
+  static constexpr uint32_t kThreads = kSfWarp ? 224 : 192;
   // per 128-byte K chunk
   static constexpr uint32_t kChunkA = 128 * 128;
   static constexpr uint32_t kBRows = CG == 1 ? 256 : 128;
@@ -124,8 +133,8 @@ struct SmemPlan {
   static constexpr uint32_t kSfbOff = kSfaOff + STAGES * kSfaBytes;
   static constexpr uint32_t kEpiOff = ((kSfbOff + STAGES * kSfbBytes) + 1023u) & ~1023u;
   static constexpr uint32_t kBarOff = kEpiOff + 4 * kEpiBufs * kEpiBufBytes;
-  // full[S], empty[S], acc_full[2], acc_empty[2], ovl, drain, fixup[4]
-  static constexpr uint32_t kNumBars = 2 * STAGES + 10;
+  // full[S], empty[S], acc_full[2], acc_empty[2], ovl, drain, fixup[4], scales[2]
+  static constexpr uint32_t kNumBars = 2 * STAGES + 12;
   static constexpr uint32_t kMiscOff = kBarOff + kNumBars * 8;  // tmem slot, abort flag
   static constexpr uint32_t kBytes = kMiscOff + 16;
   // The carve-up starts on a 1024-byte boundary (128-byte-swizzled TMA tiles).
@@ -140,11 +149,24 @@ struct SmemPlan {
   // bytes the TMA lands per chunk on the leader's full barrier (both CTAs)
   static constexpr uint32_t kChunkTx = CG * (kChunkA + kChunkB + kChunkSfa + kChunkSfb);
 
-  // TMEM columns: two accumulators (overlapping by 32 columns when scale
-  // factors need room) and the scale-factor slots.
-  static constexpr uint32_t kAccStride = kScaled ? 224 : 256;
-  static constexpr uint32_t kSfaCol = 480;
-  static constexpr uint32_t kSfbCol = 488;
+  // TMEM columns. Block-scaled kinds keep kSfSlots scale-factor slots (one
+  // stage each) at the top of the 512 columns: per chunk c and 4-scale group
+  // g, SFA takes 4 columns at (c * kGps + g) * 4 and SFB (256 rows) 8 columns
+  // after all SFA columns. The two accumulators then overlap by kOvlChunks
+  // 32-column chunks, which the epilogue drains first.
+  static constexpr uint32_t kSfaSlotCols = kScaled ? kKChunks * kGps * 4 : 0;
+  static constexpr uint32_t kSfSlotCols =
+      kScaled ? ((kSfSlots * (kKChunks * kGps * 12) + 31) / 32 * 32) / kSfSlots : 0;
+  static constexpr uint32_t kSfBase = 512 - kSfSlots * kSfSlotCols;
+  static constexpr uint32_t kAccStride = kScaled ? kSfBase - 256 : 256;
+  static constexpr uint32_t kOvlChunks = (256 - kAccStride) / 32;
+  static_assert(kAccStride % 32 == 0 && kOvlChunks < 8, "TMEM column plan");
+  __device__ static constexpr uint32_t sfa_col(uint32_t slot, int c, int g) {
+    return kSfBase + slot * kSfSlotCols + static_cast<uint32_t>(c * kGps + g) * 4;
+  }
+  __device__ static constexpr uint32_t sfb_col(uint32_t slot, int c, int g) {
+    return kSfBase + slot * kSfSlotCols + kSfaSlotCols + static_cast<uint32_t>(c * kGps + g) * 8;
+  }
 };
 
 __device__ __forceinline__ void report_status(const GemmParams& p, int code) {
@@ -232,7 +254,8 @@ __device__ __forceinline__ size_t flag_index(int32_t unit, uint32_t rank, uint32
 }
 
 template <int KIND, int CG, int STAGES, bool OUT_BF16>
-__global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ GemmParams p) {
+__global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
+    gemm_kernel(const __grid_constant__ GemmParams p) {
   using SP = SmemPlan<KIND, CG, STAGES>;
   constexpr bool kScaled = SP::kScaled;
   constexpr int kGps = SP::kGps;
@@ -260,6 +283,7 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ge
   const uint32_t ovl_bar = bar0 + 8u * (2 * STAGES + 4);
   const uint32_t drain_bar = bar0 + 8u * (2 * STAGES + 5);
   auto fix_bar = [&](uint32_t q) { return bar0 + 8u * (2 * STAGES + 6 + q); };
+  auto sf_bar = [&](uint32_t slot) { return bar0 + 8u * (2 * STAGES + 10 + slot); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SP::kMiscOff);
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + SP::kMiscOff + 4);
 
@@ -275,6 +299,7 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ge
     mbar_init(ovl_bar, 4 * CG);
     mbar_init(drain_bar, 1);
     for (uint32_t q = 0; q < 4; ++q) mbar_init(fix_bar(q), 1);
+    for (uint32_t slot = 0; slot < 2; ++slot) mbar_init(sf_bar(slot), 1);
     *abort_flag = 0u;
     fence_mbarrier_init();
     prefetch_tensormap(&p.tmA);
@@ -399,6 +424,15 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ge
             alive = false;
             break;
           }
+          const uint32_t slot = SP::kSfWarp ? (it & 1u) : 0u;
+          if constexpr (SP::kSfWarp) {
+            // this stage's scale factors, copied into `slot` by the scale copier
+            if (!wait_phase_fast<false>(sf_bar(slot), (it >> 1) & 1u, abort_flag, p,
+                                        B2G_SITE_SCALES)) {
+              alive = false;
+              break;
+            }
+          }
           tc_fence_after();
           const int32_t nc = min(kKChunks, p.k_chunks - k * kKChunks);
 #pragma unroll
@@ -408,17 +442,17 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ge
           const uint32_t b_addr = sbase + SP::kBOff + s * SP::kBBytes + c * SP::kChunkB;
           const uint64_t adesc = sdesc_kmajor_sw128(a_addr);
           const uint64_t bdesc = sdesc_kmajor_sw128(b_addr);
-          if constexpr (kScaled) {
-            // scale factors of this chunk: smem -> TMEM (in issue order with the MMAs)
+          if constexpr (kScaled && !SP::kSfWarp) {
+            // scale factors of this chunk: smem -> TMEM, in issue order with the MMAs
             const uint32_t sfa_addr = sbase + SP::kSfaOff + s * SP::kSfaBytes + c * SP::kChunkSfa;
             const uint32_t sfb_addr = sbase + SP::kSfbOff + s * SP::kSfbBytes + c * SP::kChunkSfb;
 #pragma unroll
             for (int g = 0; g < kGps; ++g) {
-              tmem_cp_32x128b_x4<CG>(tmem_base + SP::kSfaCol + 4 * g,
+              tmem_cp_32x128b_x4<CG>(tmem_base + SP::sfa_col(0, c, g),
                                      sdesc_rows16(sfa_addr + g * 512));
 #pragma unroll
               for (int rb = 0; rb < 2; ++rb)
-                tmem_cp_32x128b_x4<CG>(tmem_base + SP::kSfbCol + 8 * g + 4 * rb,
+                tmem_cp_32x128b_x4<CG>(tmem_base + SP::sfb_col(0, c, g) + 4 * rb,
                                        sdesc_rows16(sfb_addr + (rb * kGps + g) * 512));
             }
           }
@@ -433,10 +467,10 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ge
             } else if constexpr (KIND == kKindE5M2) {
               mma_f8f6f4<CG>(d_tmem, ad, bd, make_idesc<KIND, CG>(0), acc);
             } else {
-              const uint32_t g = KIND == kKindMXFP4 ? (j >> 1) : 0u;
+              const int g = KIND == kKindMXFP4 ? static_cast<int>(j >> 1) : 0;
               const uint32_t sf_id = KIND == kKindMXFP4 ? ((j & 1u) * 2u) : j;
-              const uint32_t sfa_t = (tmem_base + SP::kSfaCol + 4 * g) | (sf_id << 30);
-              const uint32_t sfb_t = (tmem_base + SP::kSfbCol + 8 * g) | (sf_id << 30);
+              const uint32_t sfa_t = (tmem_base + SP::sfa_col(slot, c, g)) | (sf_id << 30);
+              const uint32_t sfb_t = (tmem_base + SP::sfb_col(slot, c, g)) | (sf_id << 30);
               if constexpr (KIND == kKindMXFP4)
                 mma_mxf4<CG>(d_tmem, ad, bd, make_idesc<KIND, CG>(sf_id), sfa_t, sfb_t, acc);
               else
@@ -461,6 +495,62 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ge
       uint32_t spins = 0;
       while (!mbar_try_wait(drain_bar, 0) && spins < (1u << 22)) ++spins;
     }
+  } else if (warp == 6) {
+    // -------------------------------------------------------- scale copier --
+    if constexpr (SP::kSfWarp) {
+      if (leader && lane == 0) {
+        uint32_t it = 0;
+        WorkCursor cur = cursor_begin(p.plan, unit);
+        WorkItem w;
+        bool alive = true;
+        while (alive && cursor_next(p.plan, unit, cur, w)) {
+          for (int32_t k = w.k_begin; k < w.k_end; ++k, ++it) {
+            const uint32_t s = it % STAGES, ph = (it / STAGES) & 1u;
+            const uint32_t slot = it & 1u;
+            if (!wait_phase_fast<false>(full_bar(s), ph, abort_flag, p, B2G_SITE_FULL)) {
+              alive = false;
+              break;
+            }
+            if (it >= 2) {
+              // the MMAs of two stages back read this slot: their completion
+              // is the ring's empty barrier for that stage
+              const uint32_t i2 = it - 2;
+              if (!wait_phase_fast<false>(empty_bar(i2 % STAGES), (i2 / STAGES) & 1u, abort_flag,
+                                          p, B2G_SITE_EMPTY)) {
+                alive = false;
+                break;
+              }
+            }
+            tc_fence_after();
+            const int32_t nc = min(kKChunks, p.k_chunks - k * kKChunks);
+#pragma unroll
+            for (int32_t c = 0; c < kKChunks; ++c) {
+              if (c >= nc) break;
+              const uint32_t sfa_addr =
+                  sbase + SP::kSfaOff + s * SP::kSfaBytes + c * SP::kChunkSfa;
+              const uint32_t sfb_addr =
+                  sbase + SP::kSfbOff + s * SP::kSfbBytes + c * SP::kChunkSfb;
+#pragma unroll
+              for (int g = 0; g < kGps; ++g) {
+                tmem_cp_32x128b_x4<CG>(tmem_base + SP::sfa_col(slot, c, g),
+                                       sdesc_rows16(sfa_addr + g * 512));
+#pragma unroll
+                for (int rb = 0; rb < 2; ++rb)
+                  tmem_cp_32x128b_x4<CG>(tmem_base + SP::sfb_col(slot, c, g) + 4 * rb,
+                                         sdesc_rows16(sfb_addr + (rb * kGps + g) * 512));
+              }
+            }
+            tc_commit<CG>(sf_bar(slot));
+          }
+        }
+        // Drain: this thread's copies complete before TMEM can be freed.
+        if (it > 0) {
+          const uint32_t last = it - 1;
+          uint32_t spins = 0;
+          while (!mbar_try_wait(sf_bar(last & 1u), (last >> 1) & 1u) && spins < (1u << 22)) ++spins;
+        }
+      }
+    }
   } else {
     // ------------------------------------------------------------ epilogue --
     const uint32_t quad = warp & 3u;
@@ -477,8 +567,8 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ge
       const uint32_t tbase = tmem_base + ((quad * 32u) << 16) + b * SP::kAccStride;
       const int32_t m0 = w.tm * (128 * CG) + static_cast<int32_t>(rank) * 128 + quad * 32;
       const int32_t n0 = w.tn * 256;
-      // with overlapping accumulators the shared 32 columns are drained first
-      const uint32_t first_chunk = kScaled ? (b == 0 ? 7u : 0u) : 0u;
+      // with overlapping accumulators the shared chunks are drained first
+      const uint32_t first_chunk = kScaled ? (b == 0 ? 8u - SP::kOvlChunks : 0u) : 0u;
       // A split item that is this unit's last one finds the operand ring idle
       // (all its loads were consumed): each epilogue warp then moves its 32 x
       // 256 fp32 partial through its own 32 KB of the ring with bulk TMA copies
@@ -523,7 +613,7 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ge
         tmem_ld_32x32b_x32(tbase + c * 32u, v);
         tmem_wait_ld();
         if constexpr (kScaled) {
-          if (ci == 0) {
+          if (ci == SP::kOvlChunks - 1) {
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {

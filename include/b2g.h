@@ -82,6 +82,7 @@ extern "C" {
 #define B2G_SITE_ACC_FULL 4       /* epilogue waiting for a finished accumulator */
 #define B2G_SITE_OVERLAP 5        /* MMA waiting for the shared accumulator columns */
 #define B2G_SITE_FLAG 6           /* stream-K owner waiting for a contributor */
+#define B2G_SITE_SCALES 7         /* MMA waiting for scale factors copied into TMEM */
 #define B2G_STATUS_SMEM_BASE 0x2000 /* kernel returned at entry: shared memory base misaligned */
 
 /* Library ABI version (major * 100 + minor). */
