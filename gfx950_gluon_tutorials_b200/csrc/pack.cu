@@ -11,50 +11,34 @@
 //     stored as a (rows, K/32) tensor of any strides; the reference's own are
 //     M-contiguous, (1, rows_pad) (a4w4/bench.py:138-144);
 //   - e5m2 bytes with the rounding of torch's float -> float8_e5m2 cast.
-// All kernels are HBM-bound streaming passes: coalesced 16-byte loads, one
-// thread per 8 source elements.
+// All kernels are HBM-bound streaming passes (several 16-byte loads in flight
+// per lane); the element conversions use the hardware cvt instructions.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
+#include <cstring>
 
 #include "pack.cuh"
 
 namespace b2g {
 
-// fp32 -> e5m2, round to nearest even, no saturation (overflow -> inf,
-// NaN -> 0x7F with the sign kept). e5m2: bias 15, normals from 2^-14,
-// subnormals m * 2^-16 (m = 1..3), largest finite 57344.
-__device__ __forceinline__ uint32_t e5m2_from_f32(float y) {
-  const uint32_t u = __float_as_uint(y);
-  const uint32_t sign = (u >> 24) & 0x80u;
-  uint32_t a = u & 0x7FFFFFFFu;
-  if (a > 0x7F800000u) return sign | 0x7Fu;   // NaN
-  if (a >= 0x47700000u) return sign | 0x7Cu;  // >= 61440 (the tie above 57344) and inf
-  if (a >= 0x38800000u) {                     // >= 2^-14: normal
-    a += 0x000FFFFFu + ((a >> 21) & 1u);      // round the 21 dropped bits, ties to even
-    return sign | (((a >> 23) - 112u) << 2) | ((a >> 21) & 3u);
-  }
-  // below 2^-14: integer multiple of 2^-16, the value 4 being 2^-14 itself
-  const float v = __uint_as_float(a) * 65536.0f;
-  return sign | static_cast<uint32_t>(rintf(v));
-}
-
-// |y| -> e2m1 magnitude code (0..7), round to nearest even, saturating at 6.
-__device__ __forceinline__ uint32_t e2m1_mag_code(float a) {
-  if (a <= 0.25f) return 0u;
-  if (a < 0.75f) return 1u;
-  if (a <= 1.25f) return 2u;
-  if (a < 1.75f) return 3u;
-  if (a <= 2.5f) return 4u;
-  if (a < 3.5f) return 5u;
-  if (a <= 5.0f) return 6u;
-  return 7u;
-}
-
-__device__ __forceinline__ uint32_t e2m1_from_f32(float y) {
-  return ((__float_as_uint(y) >> 28) & 0x8u) | e2m1_mag_code(fabsf(y));
+// Load flavour of the streaming passes (build macro B2G_PACK_LOAD: 0 plain,
+// 1 read-only path, 2 evict-first streaming).
+#ifndef B2G_PACK_LOAD
+#define B2G_PACK_LOAD 0
+#endif
+template <typename T>
+__device__ __forceinline__ T stream_load(const T* p) {
+#if B2G_PACK_LOAD == 1
+  return __ldg(p);
+#elif B2G_PACK_LOAD == 2
+  return __ldcs(p);
+#else
+  return *p;
+#endif
 }
 
 // floor(log2(a)) for a finite a > 0 (exact, from the bits).
@@ -71,95 +55,164 @@ __device__ __forceinline__ float exp2i(int32_t n) {
   return __uint_as_float(0x00400000u);  // 2^-127
 }
 
+// Hardware conversions (sm_100a). cvt.rn.satfinite rounds to nearest even
+// and saturates finite overflow to the largest finite code; `hi` lands in the
+// upper half of the result.
+__device__ __forceinline__ uint32_t cvt_e2m1x2(float lo, float hi) {
+  uint32_t r;
+  asm("{\n\t.reg .b8 t;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 t, %2, %1;\n\t"
+      "cvt.u32.u8 %0, t;\n\t}"
+      : "=r"(r)
+      : "f"(lo), "f"(hi));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t cvt_e5m2x2_satfinite(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e5m2x2.f32 %0, %2, %1;" : "=h"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+
+// torch's float -> float8_e5m2 cast does not saturate: magnitudes from 61440
+// (the rounding midpoint above 57344) up, infinities included, become
+// infinity, and a NaN keeps its sign (0x7F | sign).
+__device__ __forceinline__ uint32_t e5m2_fix(uint32_t code, float y) {
+  const uint32_t u = __float_as_uint(y);
+  const uint32_t sign = (u >> 24) & 0x80u;
+  const uint32_t a = u & 0x7FFFFFFFu;
+  code = a >= 0x47700000u ? (sign | 0x7Cu) : code;
+  return a > 0x7F800000u ? (sign | 0x7Fu) : code;
+}
+
+__device__ __forceinline__ uint32_t e5m2x4(float a, float b, float c, float d) {
+  const uint32_t lo = cvt_e5m2x2_satfinite(a, b), hi = cvt_e5m2x2_satfinite(c, d);
+  return e5m2_fix(lo & 0xFFu, a) | (e5m2_fix(lo >> 8, b) << 8) | (e5m2_fix(hi & 0xFFu, c) << 16) |
+         (e5m2_fix(hi >> 8, d) << 24);
+}
+
 // ------------------------------------------------------------------ MXFP4 --
-// Four lanes per 32-element block, eight elements per lane.
-__global__ void quant_mxfp4_kernel(const float* __restrict__ src, int64_t ld, int32_t rows,
-                                   int32_t K, uint8_t* __restrict__ q, int64_t ldq,
-                                   uint8_t* __restrict__ sc, int64_t s0, int64_t s1) {
-  const int64_t blocks_per_row = K / 32;
-  const int64_t total = static_cast<int64_t>(rows) * blocks_per_row * 4;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  const int64_t warp_base = (static_cast<int64_t>(blockIdx.x) * blockDim.x) + (threadIdx.x & ~31u);
+// A warp takes segments of 256 elements (8 blocks of 32) of one row; four
+// lanes share a block, eight elements (32 bytes) each. kSegs segments per
+// warp iteration keep 32 * kSegs bytes per lane in flight. IDX is the index
+// type (32-bit unless the segment count needs 64).
+template <typename IDX, int kSegs>
+__global__ void __launch_bounds__(256) quant_mxfp4_kernel(const float* __restrict__ src,
+                                                          int64_t ld, int32_t rows, int32_t K,
+                                                          uint8_t* __restrict__ q, int64_t ldq,
+                                                          uint8_t* __restrict__ sc, int64_t s0,
+                                                          int64_t s1) {
+  const IDX blocks_per_row = static_cast<IDX>(K / 32);
+  const IDX segs_per_row = (blocks_per_row + 7) / 8;
+  const IDX total = static_cast<IDX>(rows) * segs_per_row;
+  const IDX nwarps = static_cast<IDX>(gridDim.x) * (blockDim.x / 32);
   const uint32_t lane = threadIdx.x & 31u;
-  for (int64_t wb = warp_base; wb < total; wb += stride) {  // uniform per warp
-    const int64_t i = wb + lane;
-    const bool active = i < total;
-    const int64_t blk = i >> 2;
-    const int32_t part = static_cast<int32_t>(i & 3);
-    const int64_t row = active ? blk / blocks_per_row : 0;
-    const int64_t jb = active ? blk - row * blocks_per_row : 0;
-    const int64_t k0 = jb * 32 + part * 8;
-    float x[8];
-    if (active) {
-      const float4* p = reinterpret_cast<const float4*>(src + row * ld + k0);
-      const float4 lo = __ldcs(p), hi = __ldcs(p + 1);
-      x[0] = lo.x; x[1] = lo.y; x[2] = lo.z; x[3] = lo.w;
-      x[4] = hi.x; x[5] = hi.y; x[6] = hi.z; x[7] = hi.w;
-    } else {
+  const IDX jl = static_cast<IDX>(lane >> 2);  // block within the segment
+  const int32_t part = static_cast<int32_t>(lane & 3u);
+  for (IDX seg0 = static_cast<IDX>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+       seg0 < total; seg0 += nwarps * kSegs) {  // uniform per warp
+    float x[kSegs][8];
+    IDX row[kSegs], jb[kSegs];
+    bool on[kSegs];
 #pragma unroll
-      for (int t = 0; t < 8; ++t) x[t] = 0.0f;
-    }
-    float amax = 0.0f;
-    uint32_t nonfinite = 0;
+    for (int u = 0; u < kSegs; ++u) {
+      const IDX seg = seg0 + static_cast<IDX>(u) * nwarps;
+      row[u] = seg / segs_per_row;
+      jb[u] = (seg - row[u] * segs_per_row) * 8 + jl;
+      on[u] = seg < total && jb[u] < blocks_per_row;
+      if (on[u]) {
+        const float4* p = reinterpret_cast<const float4*>(
+            src + static_cast<int64_t>(row[u]) * ld + static_cast<int64_t>(jb[u]) * 32 + part * 8);
+        const float4 lo = stream_load(p), hi = stream_load(p + 1);
+        x[u][0] = lo.x; x[u][1] = lo.y; x[u][2] = lo.z; x[u][3] = lo.w;
+        x[u][4] = hi.x; x[u][5] = hi.y; x[u][6] = hi.z; x[u][7] = hi.w;
+      } else {
 #pragma unroll
-    for (int t = 0; t < 8; ++t) {
-      const float a = fabsf(x[t]);
-      nonfinite |= (__float_as_uint(a) >= 0x7F800000u) ? 1u : 0u;
-      amax = fmaxf(amax, a);
+        for (int t = 0; t < 8; ++t) x[u][t] = 0.0f;
+      }
     }
 #pragma unroll
-    for (int o = 1; o < 4; o <<= 1) {
-      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-      nonfinite |= __shfl_xor_sync(0xffffffffu, nonfinite, o);
-    }
-    uint32_t sbyte, packed = 0;
-    if (nonfinite) {
-      sbyte = 255u;
-    } else if (amax == 0.0f) {
-      sbyte = 0u;
-      // scale 2^-127: every element rounds to a (signed) zero code
+    for (int u = 0; u < kSegs; ++u) {
+      float amax = 0.0f;
 #pragma unroll
-      for (int t = 0; t < 8; ++t) packed |= ((__float_as_uint(x[t]) >> 28) & 0x8u) << (4 * t);
-    } else {
-      int32_t s = floor_log2_f32(amax) - 2;
-      if (s < -127) s = -127;
-      sbyte = static_cast<uint32_t>(s + 127);
-      const float mul = exp2i(-s);
+      for (int t = 0; t < 8; ++t) amax = fmaxf(amax, fabsf(x[u][t]));
+      // fmaxf drops NaN: flag non-finite elements separately
+      uint32_t nonfinite = 0;
 #pragma unroll
-      for (int t = 0; t < 8; ++t) packed |= e2m1_from_f32(x[t] * mul) << (4 * t);
-    }
-    if (active) {
-      *reinterpret_cast<uint32_t*>(q + row * ldq + (k0 >> 1)) = packed;
-      if (part == 0) sc[row * s0 + jb * s1] = static_cast<uint8_t>(sbyte);
+      for (int t = 0; t < 8; ++t) nonfinite |= (__float_as_uint(x[u][t]) & 0x7F800000u) == 0x7F800000u;
+#pragma unroll
+      for (int o = 1; o < 4; o <<= 1) {
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        nonfinite |= __shfl_xor_sync(0xffffffffu, nonfinite, o);
+      }
+      uint32_t sbyte, packed = 0;
+      if (nonfinite) {
+        sbyte = 255u;
+      } else if (amax == 0.0f) {
+        sbyte = 0u;  // scale 2^-127: every element rounds to a (signed) zero code
+#pragma unroll
+        for (int t = 0; t < 8; ++t) packed |= ((__float_as_uint(x[u][t]) >> 28) & 0x8u) << (4 * t);
+      } else {
+        int32_t sx = floor_log2_f32(amax) - 2;
+        if (sx < -127) sx = -127;
+        sbyte = static_cast<uint32_t>(sx + 127);
+        const float mul = exp2i(-sx);
+#pragma unroll
+        for (int t = 0; t < 8; t += 2)
+          packed |= cvt_e2m1x2(x[u][t] * mul, x[u][t + 1] * mul) << (4 * t);
+      }
+      if (on[u]) {
+        const int64_t r = static_cast<int64_t>(row[u]), j = static_cast<int64_t>(jb[u]);
+        *reinterpret_cast<uint32_t*>(q + r * ldq + j * 16 + part * 4) = packed;
+        if (part == 0) sc[r * s0 + j * s1] = static_cast<uint8_t>(sbyte);
+      }
     }
   }
 }
 
 // ------------------------------------------------------------ scaled e5m2 --
-__global__ void quant_mxe5m2_kernel(const float* __restrict__ src, int64_t ld, int32_t rows,
-                                    int32_t K, const uint8_t* __restrict__ sc, int64_t s0,
-                                    int64_t s1, uint8_t* __restrict__ q, int64_t ldq) {
-  const int64_t per_row = K / 8;
-  const int64_t total = static_cast<int64_t>(rows) * per_row;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-       i += stride) {
-    const int64_t row = i / per_row;
-    const int64_t k0 = (i - row * per_row) * 8;
-    const uint32_t e = sc[row * s0 + (k0 >> 5) * s1];
-    const float4* p = reinterpret_cast<const float4*>(src + row * ld + k0);
-    const float4 lo = __ldcs(p), hi = __ldcs(p + 1);
-    const float x[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
-    uint32_t w0 = 0, w1 = 0;
-    if (e != 255u) {
-      const float mul = exp2i(127 - static_cast<int32_t>(e));
+// One thread per 8 elements (32 bytes loaded), kUnroll groups per iteration.
+template <typename IDX, int kUnroll>
+__global__ void __launch_bounds__(256) quant_mxe5m2_kernel(const float* __restrict__ src,
+                                                           int64_t ld, int32_t rows, int32_t K,
+                                                           const uint8_t* __restrict__ sc,
+                                                           int64_t s0, int64_t s1,
+                                                           uint8_t* __restrict__ q, int64_t ldq) {
+  const IDX per_row = static_cast<IDX>(K / 8);
+  const IDX total = static_cast<IDX>(rows) * per_row;
+  const IDX stride = static_cast<IDX>(gridDim.x) * blockDim.x;
+  for (IDX i0 = static_cast<IDX>(blockIdx.x) * blockDim.x + threadIdx.x; i0 < total;
+       i0 += stride * kUnroll) {
+    float x[kUnroll][8];
+    uint32_t e[kUnroll];
+    int64_t row[kUnroll], k0[kUnroll];
+    bool on[kUnroll];
 #pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        w0 |= e5m2_from_f32(x[t] * mul) << (8 * t);
-        w1 |= e5m2_from_f32(x[t + 4] * mul) << (8 * t);
+    for (int u = 0; u < kUnroll; ++u) {
+      const IDX i = i0 + static_cast<IDX>(u) * stride;
+      on[u] = i < total;
+      const IDX r = on[u] ? i / per_row : 0;
+      row[u] = static_cast<int64_t>(r);
+      k0[u] = static_cast<int64_t>(i - r * per_row) * 8;
+      if (on[u]) {
+        e[u] = sc[row[u] * s0 + (k0[u] >> 5) * s1];
+        const float4* p = reinterpret_cast<const float4*>(src + row[u] * ld + k0[u]);
+        const float4 lo = stream_load(p), hi = stream_load(p + 1);
+        x[u][0] = lo.x; x[u][1] = lo.y; x[u][2] = lo.z; x[u][3] = lo.w;
+        x[u][4] = hi.x; x[u][5] = hi.y; x[u][6] = hi.z; x[u][7] = hi.w;
       }
     }
-    *reinterpret_cast<uint2*>(q + row * ldq + k0) = make_uint2(w0, w1);
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      if (!on[u]) continue;
+      uint32_t w0 = 0, w1 = 0;
+      if (e[u] != 255u) {
+        const float mul = exp2i(127 - static_cast<int32_t>(e[u]));
+        w0 = e5m2x4(x[u][0] * mul, x[u][1] * mul, x[u][2] * mul, x[u][3] * mul);
+        w1 = e5m2x4(x[u][4] * mul, x[u][5] * mul, x[u][6] * mul, x[u][7] * mul);
+      }
+      *reinterpret_cast<uint2*>(q + row[u] * ldq + k0[u]) = make_uint2(w0, w1);
+    }
   }
 }
 
@@ -179,9 +232,44 @@ template <typename T>
 __global__ void cast_e5m2_kernel(const T* __restrict__ src, int64_t n, uint8_t* __restrict__ dst) {
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
-    dst[i] = static_cast<uint8_t>(e5m2_from_f32(to_f32<T>(src[i])));
+  {
+    const float y = to_f32<T>(src[i]);
+    dst[i] = static_cast<uint8_t>(e5m2_fix(cvt_e5m2x2_satfinite(y, 0.0f) & 0xFFu, y));
+  }
 }
 
+// Four elements per thread and group: one 16-byte (fp32) or 8-byte (fp16 /
+// bf16) load and one 4-byte store; kUnroll groups in flight per thread. Needs
+// n % 4 == 0 and aligned pointers.
+template <typename T, int kUnroll>
+__global__ void __launch_bounds__(256) cast_e5m2_x4_kernel(const T* __restrict__ src, int64_t n4,
+                                                           uint32_t* __restrict__ dst) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i0 < n4;
+       i0 += stride * kUnroll) {
+    float v[kUnroll][4];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t i = i0 + u * stride;
+      if (i >= n4) continue;
+      if constexpr (sizeof(T) == 4) {
+        const float4 f = stream_load(reinterpret_cast<const float4*>(src) + i);
+        v[u][0] = f.x; v[u][1] = f.y; v[u][2] = f.z; v[u][3] = f.w;
+      } else {
+        const uint2 h = stream_load(reinterpret_cast<const uint2*>(src) + i);
+        T t[4];
+        memcpy(t, &h, sizeof(h));
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[u][j] = to_f32<T>(t[j]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t i = i0 + u * stride;
+      if (i < n4) dst[i] = e5m2x4(v[u][0], v[u][1], v[u][2], v[u][3]);
+    }
+  }
+}
 
 // ------------------------------------------------------- scale relayout --
 // (rows, K/32) E8M0 bytes of any strides -> blocked layout: for 128-row block
@@ -198,46 +286,45 @@ struct RelayoutArgs {
   uint8_t* dst;
 };
 
-__global__ void sf_relayout_kernel(RelayoutArgs a, RelayoutArgs b, int32_t kscales,
-                                   int32_t groups) {
-  const int64_t n_a = static_cast<int64_t>(a.row_blocks) * groups * 32;
-  const int64_t total = n_a + static_cast<int64_t>(b.row_blocks) * groups * 32;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-       i += stride) {
+template <typename IDX>
+__global__ void __launch_bounds__(256) sf_relayout_kernel(RelayoutArgs a, RelayoutArgs b,
+                                                          int32_t kscales, int32_t groups) {
+  const IDX n_a = static_cast<IDX>(a.row_blocks) * groups * 32;
+  const IDX total = n_a + static_cast<IDX>(b.row_blocks) * groups * 32;
+  const IDX stride = static_cast<IDX>(gridDim.x) * blockDim.x;
+  for (IDX i = static_cast<IDX>(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
     const bool is_a = i < n_a;
     const RelayoutArgs& t = is_a ? a : b;
-    const int64_t li = is_a ? i : i - n_a;
+    const IDX li = is_a ? i : i - n_a;
     const int32_t r0 = static_cast<int32_t>(li & 31);
-    const int64_t q = li >> 5;
-    const int32_t g = static_cast<int32_t>(q % groups);
-    const int64_t rb = q / groups;
-    uint32_t w[4];
+    const IDX qa = li >> 5;
+    const IDX rb = qa / static_cast<IDX>(groups);
+    const int32_t g = static_cast<int32_t>(qa - rb * static_cast<IDX>(groups));
+    const int64_t row0 = static_cast<int64_t>(rb) * 128 + r0;
+    uint32_t v[4][4];
 #pragma unroll
     for (int r1 = 0; r1 < 4; ++r1) {
-      const int64_t row = rb * 128 + r1 * 32 + r0;
-      uint32_t word = 0;
+      const int64_t row = row0 + r1 * 32;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int32_t k = g * 4 + j;
-        const uint32_t v =
-            (row < t.rows && k < kscales) ? __ldg(t.src + row * t.s0 + k * t.s1) : 127u;
-        word |= v << (8 * j);
+        v[r1][j] = (row < t.rows && k < kscales) ? __ldg(t.src + row * t.s0 + k * t.s1) : 127u;
       }
-      w[r1] = word;
     }
-    *reinterpret_cast<uint4*>(t.dst + (rb * groups + g) * 512 + r0 * 16) =
+    uint32_t w[4];
+#pragma unroll
+    for (int r1 = 0; r1 < 4; ++r1)
+      w[r1] = v[r1][0] | (v[r1][1] << 8) | (v[r1][2] << 16) | (v[r1][3] << 24);
+    *reinterpret_cast<uint4*>(t.dst + (static_cast<int64_t>(rb) * groups + g) * 512 + r0 * 16) =
         make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
 
+// Enough CTAs to cover `work` items once (the block scheduler balances the
+// waves); the kernels' grid-stride loops only matter past the grid limit.
 static int grid_for(int64_t work, int threads) {
-  int dev = 0, sms = 148;
-  if (cudaGetDevice(&dev) == cudaSuccess)
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   int64_t blocks = (work + threads - 1) / threads;
-  const int64_t cap = static_cast<int64_t>(sms) * 8;
-  if (blocks > cap) blocks = cap;
+  if (blocks > (int64_t{1} << 30)) blocks = int64_t{1} << 30;
   if (blocks < 1) blocks = 1;
   return static_cast<int>(blocks);
 }
@@ -245,23 +332,53 @@ static int grid_for(int64_t work, int threads) {
 cudaError_t launch_quant_mxfp4(const float* src, int64_t ld, int rows, int K, uint8_t* q,
                                int64_t ldq, uint8_t* sc, int64_t s0, int64_t s1,
                                cudaStream_t stream) {
-  const int64_t work = static_cast<int64_t>(rows) * (K / 32) * 4;
-  quant_mxfp4_kernel<<<grid_for(work, 256), 256, 0, stream>>>(src, ld, rows, K, q, ldq, sc, s0,
-                                                              s1);
+  constexpr int kSegs = 2;
+  const int64_t segs = static_cast<int64_t>(rows) * ((K / 32 + 7) / 8);
+  const int grid = grid_for((segs + kSegs - 1) / kSegs * 32, 256);
+  if (segs + int64_t{kSegs} * grid * 8 < (int64_t{1} << 31))
+    quant_mxfp4_kernel<uint32_t, kSegs><<<grid, 256, 0, stream>>>(src, ld, rows, K, q, ldq, sc,
+                                                                  s0, s1);
+  else
+    quant_mxfp4_kernel<int64_t, kSegs><<<grid, 256, 0, stream>>>(src, ld, rows, K, q, ldq, sc,
+                                                                 s0, s1);
   return cudaGetLastError();
 }
 
 cudaError_t launch_quant_mxe5m2(const float* src, int64_t ld, int rows, int K,
                                 const uint8_t* sc, int64_t s0, int64_t s1, uint8_t* q,
                                 int64_t ldq, cudaStream_t stream) {
+  constexpr int kUnroll = 2;
   const int64_t work = static_cast<int64_t>(rows) * (K / 8);
-  quant_mxe5m2_kernel<<<grid_for(work, 256), 256, 0, stream>>>(src, ld, rows, K, sc, s0, s1, q,
-                                                               ldq);
+  const int grid = grid_for((work + kUnroll - 1) / kUnroll, 256);
+  if (work + int64_t{kUnroll} * grid * 256 < (int64_t{1} << 31))
+    quant_mxe5m2_kernel<uint32_t, kUnroll><<<grid, 256, 0, stream>>>(src, ld, rows, K, sc, s0,
+                                                                     s1, q, ldq);
+  else
+    quant_mxe5m2_kernel<int64_t, kUnroll><<<grid, 256, 0, stream>>>(src, ld, rows, K, sc, s0,
+                                                                    s1, q, ldq);
   return cudaGetLastError();
 }
 
 cudaError_t launch_cast_e5m2(const void* src, int dtype, int64_t n, uint8_t* dst,
                              cudaStream_t stream) {
+  const size_t esz = dtype == 2 ? 4 : 2;
+  if (n % 4 == 0 && reinterpret_cast<uintptr_t>(src) % (4 * esz) == 0 &&
+      reinterpret_cast<uintptr_t>(dst) % 4 == 0) {
+    constexpr int kUnroll = 4;
+    const int64_t n4 = n / 4;
+    const int g4 = grid_for((n4 + kUnroll - 1) / kUnroll, 256);
+    uint32_t* d4 = reinterpret_cast<uint32_t*>(dst);
+    if (dtype == 2)
+      cast_e5m2_x4_kernel<float, kUnroll>
+          <<<g4, 256, 0, stream>>>(static_cast<const float*>(src), n4, d4);
+    else if (dtype == 0)
+      cast_e5m2_x4_kernel<__half, kUnroll>
+          <<<g4, 256, 0, stream>>>(static_cast<const __half*>(src), n4, d4);
+    else
+      cast_e5m2_x4_kernel<__nv_bfloat16, kUnroll>
+          <<<g4, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(src), n4, d4);
+    return cudaGetLastError();
+  }
   const int g = grid_for(n, 256);
   if (dtype == 2)
     cast_e5m2_kernel<float><<<g, 256, 0, stream>>>(static_cast<const float*>(src), n, dst);
@@ -283,7 +400,14 @@ cudaError_t launch_sf_relayout(const uint8_t* sa, int64_t sa0, int64_t sa1, int 
   if (sb == nullptr) b.row_blocks = 0;
   const int64_t work = (static_cast<int64_t>(a.row_blocks) + b.row_blocks) * groups * 32;
   if (work == 0) return cudaSuccess;
-  sf_relayout_kernel<<<grid_for(work, 256), 256, 0, stream>>>(a, b, kscales, groups);
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int grid = static_cast<int>(std::min<int64_t>(grid_for(work, 256), int64_t{sms} * 4));
+  if (work < (int64_t{1} << 31))
+    sf_relayout_kernel<uint32_t><<<grid, 256, 0, stream>>>(a, b, kscales, groups);
+  else
+    sf_relayout_kernel<int64_t><<<grid, 256, 0, stream>>>(a, b, kscales, groups);
   return cudaGetLastError();
 }
 
