@@ -170,7 +170,8 @@ def _mx_e5m2_inputs(M, N, K, seed):
 
 
 @pytest.mark.parametrize("shape", [(128, 256, 128), (256, 512, 1024), (200, 300, 96),
-                                   (1024, 768, 2048)], ids=lambda s: "x".join(map(str, s)))
+                                   (1024, 768, 2048), (256, 384, 384)],
+                         ids=lambda s: "x".join(map(str, s)))
 def test_a8w8_scaled_matches_oracle(sched, shape):
     M, N, K = shape
     xa, xb, ea, eb = _mx_e5m2_inputs(M, N, K, M * N + K)
@@ -201,7 +202,8 @@ def _reference_style_mxfp4(M, N, K, seed):
 
 
 @pytest.mark.parametrize("shape", [(128, 256, 256), (256, 512, 1024), (200, 320, 1024),
-                                   (1000, 600, 2048), (128, 256, 64)],
+                                   (1000, 600, 2048), (128, 256, 64), (256, 512, 768),
+                                   (200, 264, 1280)],
                          ids=lambda s: "x".join(map(str, s)))
 def test_a4w4_reference_style_matches_oracle(sched, shape):
     M, N, K = shape
