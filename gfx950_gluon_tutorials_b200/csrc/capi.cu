@@ -198,8 +198,11 @@ int encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t
   return r == CUDA_SUCCESS ? B2G_OK : B2G_ETENSORMAP;
 }
 
+// `after_relayout`: the scale relayout was launched just before on `stream`;
+// the GEMM may then start early (programmatic dependency) and waits for it
+// only before loading scales.
 template <int KIND, int CG, bool OB>
-int launch_gemm_t(const GemmParams& prm, int units, cudaStream_t stream) {
+int launch_gemm_t(const GemmParams& prm, int units, bool after_relayout, cudaStream_t stream) {
   constexpr bool kScaled = KindTraits<KIND>::kScaled;
   constexpr int kStages = CG == 1 ? B2G_STAGES_CG1 : (kScaled ? B2G_STAGES_CG2_SCALED : B2G_STAGES_CG2);
   using SP = SmemPlan<KIND, CG, kStages>;
@@ -220,43 +223,50 @@ int launch_gemm_t(const GemmParams& prm, int units, cudaStream_t stream) {
   cfg.blockDim = dim3(SP::kThreads, 1, 1);
   cfg.dynamicSmemBytes = SP::kDynBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
+  unsigned n_attr = 0;
   if (CG == 2) {
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    attr[n_attr].id = cudaLaunchAttributeClusterDimension;
+    attr[n_attr].val.clusterDim.x = 2;
+    attr[n_attr].val.clusterDim.y = 1;
+    attr[n_attr].val.clusterDim.z = 1;
+    ++n_attr;
   }
+  if (after_relayout) {
+    attr[n_attr].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n_attr].val.programmaticStreamSerializationAllowed = 1;
+    ++n_attr;
+  }
+  cfg.attrs = n_attr ? attr : nullptr;
+  cfg.numAttrs = n_attr;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, prm);
   return e == cudaSuccess ? B2G_OK : static_cast<int>(e);
 }
 
 template <int KIND, int CG>
-int launch_gemm_out(const GemmParams& prm, int units, int out_dtype, cudaStream_t s) {
-  return out_dtype == B2G_DT_BF16 ? launch_gemm_t<KIND, CG, true>(prm, units, s)
-                                  : launch_gemm_t<KIND, CG, false>(prm, units, s);
+int launch_gemm_out(const GemmParams& prm, int units, int out_dtype, bool dep, cudaStream_t s) {
+  return out_dtype == B2G_DT_BF16 ? launch_gemm_t<KIND, CG, true>(prm, units, dep, s)
+                                  : launch_gemm_t<KIND, CG, false>(prm, units, dep, s);
 }
 
-int dispatch(int kind, int cg, const GemmParams& prm, int units, int out_dtype,
+int dispatch(int kind, int cg, const GemmParams& prm, int units, int out_dtype, bool dep,
              cudaStream_t s) {
   switch (kind) {
     case B2G_KIND_F16:
-      return cg == 2 ? launch_gemm_out<kKindF16, 2>(prm, units, out_dtype, s)
-                     : launch_gemm_out<kKindF16, 1>(prm, units, out_dtype, s);
+      return cg == 2 ? launch_gemm_out<kKindF16, 2>(prm, units, out_dtype, dep, s)
+                     : launch_gemm_out<kKindF16, 1>(prm, units, out_dtype, dep, s);
     case B2G_KIND_BF16:
-      return cg == 2 ? launch_gemm_out<kKindBF16, 2>(prm, units, out_dtype, s)
-                     : launch_gemm_out<kKindBF16, 1>(prm, units, out_dtype, s);
+      return cg == 2 ? launch_gemm_out<kKindBF16, 2>(prm, units, out_dtype, dep, s)
+                     : launch_gemm_out<kKindBF16, 1>(prm, units, out_dtype, dep, s);
     case B2G_KIND_E5M2:
-      return cg == 2 ? launch_gemm_out<kKindE5M2, 2>(prm, units, out_dtype, s)
-                     : launch_gemm_out<kKindE5M2, 1>(prm, units, out_dtype, s);
+      return cg == 2 ? launch_gemm_out<kKindE5M2, 2>(prm, units, out_dtype, dep, s)
+                     : launch_gemm_out<kKindE5M2, 1>(prm, units, out_dtype, dep, s);
     case B2G_KIND_MXE5M2:
-      return cg == 2 ? launch_gemm_out<kKindMXE5M2, 2>(prm, units, out_dtype, s)
-                     : launch_gemm_out<kKindMXE5M2, 1>(prm, units, out_dtype, s);
+      return cg == 2 ? launch_gemm_out<kKindMXE5M2, 2>(prm, units, out_dtype, dep, s)
+                     : launch_gemm_out<kKindMXE5M2, 1>(prm, units, out_dtype, dep, s);
     case B2G_KIND_MXFP4:
-      return cg == 2 ? launch_gemm_out<kKindMXFP4, 2>(prm, units, out_dtype, s)
-                     : launch_gemm_out<kKindMXFP4, 1>(prm, units, out_dtype, s);
+      return cg == 2 ? launch_gemm_out<kKindMXFP4, 2>(prm, units, out_dtype, dep, s)
+                     : launch_gemm_out<kKindMXFP4, 1>(prm, units, out_dtype, dep, s);
     default: return B2G_EINVAL;
   }
 }
@@ -323,6 +333,7 @@ int run_gemm(const GemmCall& c) {
 
   GemmParams prm;
   std::memset(&prm, 0, sizeof(prm));
+  bool relayout = false;
   const int64_t eb = storage_elem_bytes(c.kind);
   const uint64_t rb = static_cast<uint64_t>(row_bytes(c.kind, c.K));
   rc = encode_2d(&prm.tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, c.A, rb, static_cast<uint64_t>(c.M),
@@ -345,6 +356,7 @@ int run_gemm(const GemmCall& c) {
     const uint8_t* sfb = b_blocked ? c.sfb : ws + g.sfb_off;
     if (!aligned16(sfa) || !aligned16(sfb)) return B2G_EALIGN;
     if (!a_blocked || !b_blocked) {
+      relayout = true;
       const cudaError_t e = launch_sf_relayout(
           a_blocked ? nullptr : c.sfa, c.sfa_s0, c.sfa_s1, c.M, ws + g.sfa_off,
           b_blocked ? nullptr : c.sfb, c.sfb_s0, c.sfb_s1, c.N, ws + g.sfb_off, c.K / 32,
@@ -380,7 +392,7 @@ int run_gemm(const GemmCall& c) {
   prm.prefetch = static_cast<int32_t>(g_opt.prefetch.load());
   prm.timeout_ns = static_cast<uint64_t>(g_opt.timeout_ms.load()) * 1000000ull;
   prm.k_chunks = static_cast<int32_t>((rb + 127) / 128);
-  return dispatch(c.kind, g.cg, prm, g.launched, c.out_dtype, c.stream);
+  return dispatch(c.kind, g.cg, prm, g.launched, c.out_dtype, relayout, c.stream);
 }
 
 }  // namespace

@@ -326,6 +326,7 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
     // ------------------------------------------------------------ producer --
     if (lane == 0) {
       uint32_t it = 0;
+      bool sf_dep_done = false;
       WorkCursor cur = cursor_begin(p.plan, unit);
       WorkItem w;
       bool alive = true;
@@ -376,6 +377,12 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
               tma_load_2d_pair(b_dst, &p.tmB, fb, kc * 128, b_row);
             }
             if constexpr (kScaled) {
+              // the scale relayout launched just before this grid (programmatic
+              // dependency) must have finished before the first scale load
+              if (!sf_dep_done) {
+                grid_dependency_wait();
+                sf_dep_done = true;
+              }
               // blocked scales: this CTA's 128-row group of A, both groups of the B tile
               const uint32_t sfa_dst = sbase + SP::kSfaOff + s * SP::kSfaBytes + c * SP::kChunkSfa;
               const uint32_t sfb_dst = sbase + SP::kSfbOff + s * SP::kSfbBytes + c * SP::kChunkSfb;

@@ -22,6 +22,7 @@
 #include <cstring>
 
 #include "pack.cuh"
+#include "ptx.cuh"
 
 namespace b2g {
 
@@ -289,6 +290,8 @@ struct RelayoutArgs {
 template <typename IDX>
 __global__ void __launch_bounds__(256) sf_relayout_kernel(RelayoutArgs a, RelayoutArgs b,
                                                           int32_t kscales, int32_t groups) {
+  // the GEMM that reads this output may start its prologue and operand loads
+  grid_launch_dependents();
   const IDX n_a = static_cast<IDX>(a.row_blocks) * groups * 32;
   const IDX total = n_a + static_cast<IDX>(b.row_blocks) * groups * 32;
   const IDX stride = static_cast<IDX>(gridDim.x) * blockDim.x;

@@ -122,6 +122,18 @@ __device__ __forceinline__ bool mbar_try_wait_cluster_sleep(uint32_t bar, uint32
   return ok != 0;
 }
 
+// ------------------------------------------------- dependent launches --
+// Lets a grid launched with programmatic stream serialization start once
+// every CTA of this grid has executed it (or exited).
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+// Waits until the grids this one depends on have completed and their writes
+// are visible (returns at once when launched without such a dependency).
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // -------------------------------------------------------------------- TMA --
 // 2-D tiled load into this CTA's shared memory, completing on `bar`.
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
