@@ -67,8 +67,8 @@ def tensor_peak(dtype_name: str, peaks: dict) -> float:
 class ClockSampler:
     """SM clock and throttle reasons sampled while timing.
 
-    Polls NVML from a background thread every ~2 ms (the timed region of a
-    default run is only tens of ms); falls back to `nvidia-smi -lms` when the
+    Polls NVML from a background thread about every millisecond (the timed
+    region of a default run is only tens of ms); reports the absence when the
     NVML bindings are missing."""
 
     REASONS = {  # NVML clocks-event reason bits reported as rejection criteria
@@ -106,17 +106,22 @@ class ClockSampler:
 
     def _poll(self):
         n = self.nvml
+        try:
+            smax = float(n.nvmlDeviceGetMaxClockInfo(self.handle, n.NVML_CLOCK_SM))
+        except Exception:  # noqa: BLE001
+            return
+        power, i = 0.0, 0
         while not self._stop.is_set():
             try:
                 sm = n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM)
-                smax = n.nvmlDeviceGetMaxClockInfo(self.handle, n.NVML_CLOCK_SM)
                 reasons = n.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
-                power = n.nvmlDeviceGetPowerUsage(self.handle) / 1000.0
-                self.samples.append((float(sm), float(smax), int(reasons), power,
-                                     time.perf_counter()))
+                if i % 5 == 0:  # the power reading is the slowest query
+                    power = n.nvmlDeviceGetPowerUsage(self.handle) / 1000.0
+                self.samples.append((float(sm), smax, int(reasons), power, time.perf_counter()))
             except Exception:  # noqa: BLE001
                 break
-            time.sleep(0.002)
+            i += 1
+            time.sleep(0.0005)
 
     def stop(self, window: tuple[float, float] | None = None) -> dict:
         """Summary of the samples taken inside `window` (host perf_counter times
