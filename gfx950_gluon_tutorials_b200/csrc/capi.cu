@@ -15,6 +15,7 @@
 #include "gemm_kernel.cuh"
 #include "pack.cuh"
 #include "sched.h"
+#include "skinny_kernel.cuh"
 
 using namespace b2g;
 
@@ -42,6 +43,8 @@ struct Options {
   std::atomic<int64_t> inject{0};
   std::atomic<int64_t> max_units{0};     // 0 = one unit per SM (pair)
   std::atomic<int64_t> prefetch{0};      // k-iterations pulled into L2 ahead of the ring
+  std::atomic<int64_t> skinny_max_m{128};  // swap-AB kernel up to this M (0 = never)
+  std::atomic<int64_t> skinny_splits{0};   // K splits per tile for it (0 = automatic)
 };
 Options g_opt;
 
@@ -129,6 +132,11 @@ int64_t row_bytes(int kind, int64_t K) {
 
 size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
 
+// Zero-at-rest flag words at the start of every workspace: four per SM.
+size_t flag_region_bytes(int sms) {
+  return align256(static_cast<size_t>(sms) * 4 * sizeof(uint32_t));
+}
+
 struct Geometry {
   int cg;
   SkPlan plan;
@@ -160,13 +168,13 @@ Geometry geometry(int kind, int M, int N, int K, int sms, int pair_cap = 0) {
                      static_cast<int>(g_opt.min_sk_iters.load()));
   g.launched = std::min(units, std::max(g.plan.dp_tiles, g.plan.sk_units));
   if (g.launched < 1) g.launched = 1;
-  // The flag region has one fixed size per device (every unit of every plan
-  // fits: units * cta_group <= SMs), so partial sums written by one call can
-  // never sit where a later call with another geometry looks for its flags.
+  // Every workspace starts with the same fixed-size flag region (every unit
+  // of every plan fits: units * cta_group <= SMs), reserved even by calls that
+  // use no flags, so nothing another call writes (partial sums, relaid scales)
+  // can sit where a later call looks for its flags, which must read zero.
   size_t off = 0;
   g.flags_off = off;
-  g.flags_bytes = g.plan.sk_units > 0 ? align256(static_cast<size_t>(sms) * 4 * sizeof(uint32_t))
-                                      : 0;
+  g.flags_bytes = flag_region_bytes(sms);
   off += g.flags_bytes;
   g.partial_off = off;
   g.partial_bytes = static_cast<size_t>(g.plan.sk_units) * g.cg * 128 * 256 * sizeof(float);
@@ -180,6 +188,39 @@ Geometry geometry(int kind, int M, int N, int K, int sms, int pair_cap = 0) {
   g.sfb_bytes = is_scaled(kind) ? static_cast<size_t>(blocked_scale_bytes(N, K)) : 0;
   off += align256(g.sfb_bytes);
   g.total = off;
+  return g;
+}
+
+// ------------------------------------------------------- skinny (small M) --
+bool use_skinny(int kind, int M) {
+  const int64_t lim = g_opt.skinny_max_m.load();
+  return (kind == B2G_KIND_F16 || kind == B2G_KIND_BF16 || kind == B2G_KIND_E5M2) && lim > 0 &&
+         M <= lim && M <= 128;
+}
+
+struct SkinnyGeom {
+  int bn, tiles, splits, cps, k_chunks;
+  size_t partial_off, partial_bytes, total;
+};
+
+// About one wave of (128-column tile, K split) CTAs: as many K splits as fit
+// next to the tiles on the SMs, each keeping at least 8 chunks (or
+// B2G_OPT_SKINNY_SPLITS when set).
+// Counters live in the workspace's flag region, partial tiles after it.
+SkinnyGeom skinny_geometry(int kind, int M, int N, int K, int sms) {
+  SkinnyGeom g{};
+  g.bn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128;
+  g.k_chunks = static_cast<int>((row_bytes(kind, K) + 127) / 128);
+  g.tiles = (N + 127) / 128;
+  const int64_t forced = g_opt.skinny_splits.load();
+  const int want = std::max(1, sms / g.tiles);
+  const int splits = forced > 0 ? static_cast<int>(std::min<int64_t>(forced, g.k_chunks))
+                                : std::min(want, std::max(1, g.k_chunks / 8));
+  g.cps = (g.k_chunks + splits - 1) / splits;
+  g.splits = (g.k_chunks + g.cps - 1) / g.cps;
+  g.partial_off = flag_region_bytes(sms);
+  g.partial_bytes = g.splits > 1 ? static_cast<size_t>(g.tiles) * g.splits * 128 * g.bn * 4 : 0;
+  g.total = g.partial_off + align256(g.partial_bytes);
   return g;
 }
 
@@ -271,6 +312,42 @@ int dispatch(int kind, int cg, const GemmParams& prm, int units, int out_dtype, 
   }
 }
 
+template <int KIND, int BN, bool OB>
+int launch_skinny_t(const SkinnyParams& prm, int blocks, cudaStream_t stream) {
+  using SP = SkinnyPlan<BN>;
+  auto kern = skinny_kernel<KIND, BN, OB>;
+  static std::atomic<uint64_t> attr_done{0};  // bit per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = 1ull << (dev & 63);
+  if ((attr_done.load() & bit) == 0) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(SP::kDynBytes));
+    if (e != cudaSuccess) return static_cast<int>(e);
+    attr_done.fetch_or(bit);
+  }
+  kern<<<blocks, SP::kThreads, SP::kDynBytes, stream>>>(prm);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? B2G_OK : static_cast<int>(e);
+}
+
+template <int KIND, int BN>
+int launch_skinny_out(const SkinnyParams& prm, int blocks, int out_dtype, cudaStream_t s) {
+  return out_dtype == B2G_DT_BF16 ? launch_skinny_t<KIND, BN, true>(prm, blocks, s)
+                                  : launch_skinny_t<KIND, BN, false>(prm, blocks, s);
+}
+
+template <int KIND>
+int launch_skinny_bn(const SkinnyParams& prm, int bn, int blocks, int out_dtype,
+                     cudaStream_t s) {
+  switch (bn) {
+    case 16: return launch_skinny_out<KIND, 16>(prm, blocks, out_dtype, s);
+    case 32: return launch_skinny_out<KIND, 32>(prm, blocks, out_dtype, s);
+    case 64: return launch_skinny_out<KIND, 64>(prm, blocks, out_dtype, s);
+    default: return launch_skinny_out<KIND, 128>(prm, blocks, out_dtype, s);
+  }
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 struct GemmCall {
@@ -319,6 +396,42 @@ int check_call(const GemmCall& c) {
   return B2G_OK;
 }
 
+// C = A * B^T for M <= 128 with the swap-AB kernel (skinny_kernel.cuh).
+int run_skinny(const GemmCall& c, int sms) {
+  const SkinnyGeom g = skinny_geometry(c.kind, c.M, c.N, c.K, sms);
+  if (c.ws == nullptr || c.ws_bytes < g.total) return B2G_EWORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(c.ws) & 255u) != 0) return B2G_EALIGN;
+  uint8_t* ws = static_cast<uint8_t*>(c.ws);
+  SkinnyParams prm;
+  std::memset(&prm, 0, sizeof(prm));
+  const int64_t eb = storage_elem_bytes(c.kind);
+  const uint64_t rb = static_cast<uint64_t>(row_bytes(c.kind, c.K));
+  int rc = encode_2d(&prm.tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, c.B, rb, static_cast<uint64_t>(c.N),
+                     static_cast<uint64_t>(c.ldb * eb), 128, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc != B2G_OK) return rc;
+  rc = encode_2d(&prm.tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, c.A, rb, static_cast<uint64_t>(c.M),
+                 static_cast<uint64_t>(c.lda * eb), 128, static_cast<uint32_t>(g.bn),
+                 CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc != B2G_OK) return rc;
+  prm.C = c.C;
+  prm.ldc = c.ldc;
+  prm.partials = g.partial_bytes ? reinterpret_cast<float*>(ws + g.partial_off) : nullptr;
+  prm.counters = reinterpret_cast<uint32_t*>(ws);  // inside the zero-at-rest flag region
+  prm.status = c.status;
+  prm.M = c.M;
+  prm.N = c.N;
+  prm.k_chunks = g.k_chunks;
+  prm.splits = g.splits;
+  prm.chunks_per_split = g.cps;
+  prm.timeout_ns = static_cast<uint64_t>(g_opt.timeout_ms.load()) * 1000000ull;
+  const int blocks = g.tiles * g.splits;
+  switch (c.kind) {
+    case B2G_KIND_F16: return launch_skinny_bn<0>(prm, g.bn, blocks, c.out_dtype, c.stream);
+    case B2G_KIND_BF16: return launch_skinny_bn<1>(prm, g.bn, blocks, c.out_dtype, c.stream);
+    default: return launch_skinny_bn<2>(prm, g.bn, blocks, c.out_dtype, c.stream);
+  }
+}
+
 int run_gemm(const GemmCall& c) {
   int rc = check_call(c);
   if (rc != B2G_OK) return rc;
@@ -326,6 +439,7 @@ int run_gemm(const GemmCall& c) {
   cudaGetDevice(&dev);
   const int sms = current_sms();
   if (sms <= 0) return B2G_ENODEVICE;
+  if (use_skinny(c.kind, c.M)) return run_skinny(c, sms);
   const Geometry g = geometry(c.kind, c.M, c.N, c.K, sms, pair_capacity(dev, sms));
   if (g.total > 0 && (c.ws == nullptr || c.ws_bytes < g.total)) return B2G_EWORKSPACE;
   if (c.ws != nullptr && (reinterpret_cast<uintptr_t>(c.ws) & 255u) != 0) return B2G_EALIGN;
@@ -474,6 +588,7 @@ size_t b2g_gemm_workspace_bytes(int kind, int M, int N, int K) {
   cudaGetDevice(&dev);
   const int sms = current_sms();
   if (sms <= 0) return 0;
+  if (use_skinny(kind, M)) return skinny_geometry(kind, M, N, K, sms).total;
   return geometry(kind, M, N, K, sms, pair_capacity(dev, sms)).total;
 }
 
@@ -609,6 +724,14 @@ int b2g_set_option(int key, int64_t value) {
       if (value < 0 || value > 64) return B2G_EINVAL;
       g_opt.prefetch.store(value);
       return B2G_OK;
+    case B2G_OPT_SKINNY_MAX_M:
+      if (value < 0 || value > 128) return B2G_EINVAL;
+      g_opt.skinny_max_m.store(value);
+      return B2G_OK;
+    case B2G_OPT_SKINNY_SPLITS:
+      if (value < 0 || value > 64) return B2G_EINVAL;
+      g_opt.skinny_splits.store(value);
+      return B2G_OK;
     default: return B2G_EINVAL;
   }
 }
@@ -623,6 +746,8 @@ int64_t b2g_get_option(int key) {
     case B2G_OPT_INJECT_FLAG_TIMEOUT: return g_opt.inject.load();
     case B2G_OPT_MAX_UNITS: return g_opt.max_units.load();
     case B2G_OPT_L2_PREFETCH: return g_opt.prefetch.load();
+    case B2G_OPT_SKINNY_MAX_M: return g_opt.skinny_max_m.load();
+    case B2G_OPT_SKINNY_SPLITS: return g_opt.skinny_splits.load();
     default: return -1;
   }
 }

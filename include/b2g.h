@@ -206,6 +206,12 @@ B2G_API int b2g_cast_e5m2(const void* src, int src_dtype, int64_t n, uint8_t* ds
 #define B2G_OPT_MAX_UNITS 7   /* cap on persistent work units (0 = one per SM / pair) */
 #define B2G_OPT_L2_PREFETCH 8 /* k-iterations of A/B the producer pulls into L2 ahead
                                  of its shared-memory loads (default 0 = off) */
+#define B2G_OPT_SKINNY_MAX_M 9 /* fp16 / bf16 / unscaled e5m2 GEMMs with M up to this
+                                  (default 128, at most 128; 0 = never) run the
+                                  memory-bound swap-AB kernel: B's rows on the MMA's
+                                  128-row side, A's rows on its N side */
+#define B2G_OPT_SKINNY_SPLITS 10 /* K splits per 128-column tile in that kernel
+                                    (default 0 = chosen from the SM count) */
 
 B2G_API int b2g_set_option(int key, int64_t value);
 B2G_API int64_t b2g_get_option(int key);

@@ -109,3 +109,5 @@ def test_options_roundtrip():
     finally:
         _lib.set_option(_lib.OPT_SK_MODE, old)
     assert _lib.lib().b2g_set_option(999, 1) == _lib.EINVAL
+    assert _lib.get_option(_lib.OPT_SKINNY_MAX_M) == 128
+    assert _lib.lib().b2g_set_option(_lib.OPT_SKINNY_MAX_M, 129) == _lib.EINVAL

@@ -53,10 +53,12 @@ def assert_close(c: np.ndarray, ref: np.ndarray, tol: float, ref_atol: bool = Tr
     dict(pair=1, sk=3, min_sk=1, units=9),
 ], ids=lambda d: f"pair{d['pair']}-sk{d['sk']}-min{d['min_sk']}-u{d['units']}")
 def sched(request, cuda_device):
+    """Main-kernel schedule variants; the small-M swap-AB kernel is switched off
+    so that these cases keep exercising the persistent kernel."""
     keys = {"pair": _lib.OPT_PAIR, "sk": _lib.OPT_SK_MODE, "min_sk": _lib.OPT_MIN_SK_ITERS,
-            "units": _lib.OPT_MAX_UNITS}
+            "units": _lib.OPT_MAX_UNITS, "skinny": _lib.OPT_SKINNY_MAX_M}
     old = {k: _lib.get_option(v) for k, v in keys.items()}
-    for k, v in request.param.items():
+    for k, v in dict(request.param, skinny=0).items():
         _lib.set_option(keys[k], v)
     yield request.param
     for k, v in old.items():
@@ -323,3 +325,117 @@ def test_preblocked_scales_match_per_call_relayout(cuda_device, kind):
                          out_dtype=torch.bfloat16)
     ops.check_status()
     assert torch.equal(c0, c1)
+
+
+# ------------------------------------------------------------- small M (swap-AB)
+SKINNY_SHAPES = [(1, 256, 64), (7, 1000, 136), (16, 4096, 1024), (33, 300, 2048),
+                 (64, 520, 4096), (100, 2048, 512), (128, 384, 8192), (5, 129, 40000)]
+
+
+@pytest.fixture
+def skinny_on(cuda_device):
+    old = _lib.get_option(_lib.OPT_SKINNY_MAX_M)
+    _lib.set_option(_lib.OPT_SKINNY_MAX_M, 128)
+    yield
+    _lib.set_option(_lib.OPT_SKINNY_MAX_M, old)
+    ops.check_status(cuda_device)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["fp16", "bf16"])
+@pytest.mark.parametrize("shape", SKINNY_SHAPES, ids=lambda s: "x".join(map(str, s)))
+def test_skinny_a16w16_matches_oracle(skinny_on, dtype, shape):
+    M, N, K = shape
+    g = torch.Generator(device="cuda").manual_seed(M * 5 + N + K)
+    a = torch.rand((M, K), generator=g, device="cuda", dtype=torch.float32).to(dtype) - 0.5
+    b_t = torch.rand((N, K), generator=g, device="cuda", dtype=torch.float32).to(dtype) - 0.5
+    c = a16w16.matmul(a, b_t.T)
+    ops.check_status()
+    if dtype == torch.float16:
+        ref = mx.gemm_f16_ref(a.cpu().numpy(), b_t.cpu().numpy(), "f16").astype(np.float32)
+    else:
+        ref = mx.bf16_bits_to_f32(mx.gemm_f16_ref(bits16(a), bits16(b_t), "bf16"))
+    assert_close(as_f32(c), ref, TOL_F16)
+
+
+@pytest.mark.parametrize("shape", [(1, 512, 1024), (48, 1000, 2048), (128, 256, 8192)],
+                         ids=lambda s: "x".join(map(str, s)))
+def test_skinny_a8w8_matches_oracle(skinny_on, shape):
+    M, N, K = shape
+    g = torch.Generator(device="cuda").manual_seed(M + 3 * N + K)
+    a = (torch.rand((M, K), generator=g, device="cuda").half() - 0.5).to(torch.float8_e5m2)
+    b_t = (torch.rand((N, K), generator=g, device="cuda").half() - 0.5).to(torch.float8_e5m2)
+    c = a8w8.matmul(a, b_t.T)
+    ops.check_status()
+    ref = mx.gemm_e5m2_ref(a.view(torch.uint8).cpu().numpy(),
+                           b_t.view(torch.uint8).cpu().numpy()).astype(np.float32)
+    assert_close(as_f32(c), ref, TOL_F8)
+
+
+def test_skinny_split_reduction_is_deterministic(skinny_on):
+    """Several K splits per tile add their partials in split order: repeated
+    calls give bit-identical C."""
+    g = torch.Generator(device="cuda").manual_seed(21)
+    a = torch.randn((16, 8192), generator=g, device="cuda").half()
+    b_t = torch.randn((2048, 8192), generator=g, device="cuda").half()
+    first = ops.gemm_f16(a, b_t)
+    for _ in range(5):
+        assert torch.equal(ops.gemm_f16(a, b_t), first)
+    ops.check_status()
+
+
+def test_skinny_agrees_with_the_persistent_kernel(cuda_device):
+    g = torch.Generator(device="cuda").manual_seed(8)
+    a = torch.randn((64, 4096), generator=g, device="cuda").half() / 64
+    b_t = torch.randn((3000, 4096), generator=g, device="cuda").half() / 64
+    old = _lib.get_option(_lib.OPT_SKINNY_MAX_M)
+    try:
+        _lib.set_option(_lib.OPT_SKINNY_MAX_M, 128)
+        c_skinny = ops.gemm_f16(a, b_t)
+        _lib.set_option(_lib.OPT_SKINNY_MAX_M, 0)
+        c_main = ops.gemm_f16(a, b_t)
+    finally:
+        _lib.set_option(_lib.OPT_SKINNY_MAX_M, old)
+    ops.check_status()
+    assert_close(as_f32(c_skinny), as_f32(c_main), TOL_F16, ref_atol=False)
+
+
+def test_flag_region_stays_zero_across_mixed_calls(cuda_device):
+    """One workspace shared by calls of different kinds and geometries: the
+    flag words at its start are zero after every call (unsplit scaled GEMMs,
+    split GEMMs and small-M GEMMs all keep their data after the region)."""
+    lib = _lib.lib()
+    sms = torch.cuda.get_device_properties(cuda_device).multi_processor_count
+    flag_bytes = (sms * 16 + 255) // 256 * 256
+    ws = torch.zeros(256 << 20, dtype=torch.uint8, device=cuda_device)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    stream = torch.cuda.current_stream().cuda_stream
+    g = torch.Generator(device="cuda").manual_seed(4)
+
+    def f16(M, N, K):
+        a = torch.randn((M, K), generator=g, device="cuda").half() / 32
+        b = torch.randn((N, K), generator=g, device="cuda").half() / 32
+        c = torch.empty((M, N), dtype=torch.half, device="cuda")
+        assert lib.b2g_gemm_f16(a.data_ptr(), K, b.data_ptr(), K, c.data_ptr(), N, M, N, K, 0, 0,
+                                ws.data_ptr(), ws.numel(), status.data_ptr(), stream) == 0
+        return c, (a.float() @ b.float().T)
+
+    def fp4(M, N, K):
+        qa, sa = ops.quantize_mxfp4(torch.randn((M, K), generator=g, device="cuda"))
+        qb, sb = ops.quantize_mxfp4(torch.randn((N, K), generator=g, device="cuda"))
+        c = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+        assert lib.b2g_gemm_mxf4(qa.data_ptr(), K // 2, qb.data_ptr(), K // 2, sa.data_ptr(),
+                                 sa.stride(0), sa.stride(1), sb.data_ptr(), sb.stride(0),
+                                 sb.stride(1), c.data_ptr(), N, M, N, K, 1, ws.data_ptr(),
+                                 ws.numel(), status.data_ptr(), stream) == 0
+
+    for step in (lambda: fp4(8192, 8192, 1024),      # no split tiles: scales relaid out
+                 lambda: f16(4096, 4096, 2048),      # split tiles: flags used
+                 lambda: f16(16, 4096, 8192),        # small M: split counters
+                 lambda: fp4(4096, 4096, 2048)):
+        out = step()
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0
+        assert int(ws[:flag_bytes].count_nonzero().item()) == 0
+        if out is not None:
+            c, ref = out
+            assert_close(as_f32(c), ref.cpu().numpy(), TOL_F16, ref_atol=False)
