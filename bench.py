@@ -332,6 +332,43 @@ def time_e2e(w: Workload, steps: int, warmup: int, world: int) -> tuple[float, i
     return ms, h2d, d2h
 
 
+def time_skinny(world: int, peaks: dict, peak_src: str, iters: int = 20) -> dict:
+    """Memory-bound leg: a decode-like C = A * B^T with M = 16 rows of A against
+    this rank's N-shard of the large configuration's weight matrix (N = 53248 / g,
+    K = 16384, fp16). Runs the small-M swap-AB kernel; the bound is reading B
+    once from HBM (B alone is far larger than L2)."""
+    from gfx950_gluon_tutorials_b200 import ops
+    M, N, K = 16, 53248 // world, 16384
+    dev = torch.device("cuda", torch.cuda.current_device())
+    gen = torch.Generator(device=dev).manual_seed(77)
+    a = (torch.randn((M, K), generator=gen, device=dev) / K ** 0.5).half()
+    b = (torch.randn((N, K), generator=gen, device=dev) / K ** 0.5).half()
+    c = torch.empty((M, N), dtype=torch.float16, device=dev)
+    for _ in range(3):
+        ops.gemm_f16(a, b, c)
+    barrier(world)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(iters):
+        ops.gemm_f16(a, b, c)
+    end.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(start.elapsed_time(end) / iters, world)
+    ops.check_status()
+    algo = (M * K + N * K + M * N) * 2
+    gbs = algo / (ms * 1e-3) / 1e9
+    out = {"workload": f"fp16 M={M} N={N} K={K} per GPU (decode against a weight shard)",
+           "us_per_call": ms * 1e3, "tflops_per_gpu": 2.0 * M * N * K / (ms * 1e-3) / 1e12,
+           "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"],
+                        "unit": "GB/s", "frac": gbs / peaks["hbm_gbs"],
+                        "algorithmic_bytes_per_launch": algo,
+                        "peak_source": f"{peak_src} hbm_gbs (copy)"}}
+    del a, b, c
+    torch.cuda.empty_cache()
+    return out
+
+
 def time_allgather(w: Workload, world: int, iters: int = 10) -> dict | None:
     """Separately timed NCCL all-gather of every rank's C slab into a
     [world][M][N/world] buffer in each GPU's own memory."""
@@ -419,6 +456,8 @@ def contract_main(args):
     e2e_ms, h2d, d2h = time_e2e(w, max(3, args.steps // 5), min(args.warmup, 3), world)
     e2e_val = flops_total / (e2e_ms * 1e-3) / 1e12
     gather = time_allgather(w, world)
+    skinny = None if args.no_extra or args.config == "large" else time_skinny(world, peaks,
+                                                                               peak_src)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_reference_tflops(M, n_local, K, args.cpu_budget, os.cpu_count() or 1)
@@ -471,6 +510,8 @@ def contract_main(args):
         }
         if gather is not None:
             line["allgather"] = gather
+        if skinny is not None:
+            line["skinny"] = skinny
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()
