@@ -442,6 +442,17 @@ def contract_main(args):
     results["head"] = dict(ms=ms, tflops=value)
     by_dtype = {}
     if args.config != "large" and not args.no_extra:
+        # config 1's second case: 3840 x 3840 x 8192 fp16 (225 tiles)
+        wx = Workload("fp16_3840", 3840, 3840, 8192, "fp16", sets=4, seed=55 + rank)
+        msx = time_device(wx, args.steps, args.warmup, world)
+        tf = wx.flops * world / (msx * 1e-3) / 1e12
+        by_dtype["fp16_3840x3840x8192"] = {
+            "ms_per_step": msx, "tflops": tf, "tflops_per_gpu": tf / world,
+            "pct_of_nominal_dense_peak": 100.0 * tf / world / NOMINAL_DENSE_TFLOPS["fp16"],
+            "frac_of_measured": tf / world / tensor_peak("fp16", peaks),
+            "launches_per_step": wx.launches_per_step}
+        del wx
+        torch.cuda.empty_cache()
         for dn in ("bf8", "mxfp4"):
             wx = Workload(dn, M, n_local, K, dn, sets=4, seed=99 + rank)
             msx = time_device(wx, args.steps, args.warmup, world)

@@ -136,6 +136,49 @@ def test_a16w16_full_size_sampled_rows(cuda_device):
     assert err <= TOL_F16
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["fp16", "bf16"])
+def test_a16w16_cfg1b_3840_sampled_rows(cuda_device, dtype):
+    """Config-1's second case, 3840 x 3840 x 8192 (225 tiles of 256 x 256:
+    3 full waves of 74 pairs and a 3-tile remainder): sampled rows against the
+    oracle and all rows against the exact GPU product."""
+    M = N = 3840
+    K = 8192
+    g = torch.Generator(device="cuda").manual_seed(38)
+    a = (torch.randn((M, K), generator=g, device="cuda") / K ** 0.5).to(dtype)
+    b_t = (torch.randn((N, K), generator=g, device="cuda") / K ** 0.5).to(dtype)
+    c = a16w16.matmul(a, b_t.T)
+    ops.check_status()
+    rows = torch.randperm(M, generator=torch.Generator().manual_seed(39))[:192].cuda()
+    if dtype == torch.float16:
+        ref = mx.gemm_f16_ref(a[rows].cpu().numpy(), b_t.cpu().numpy()).astype(np.float32)
+    else:
+        ref = mx.bf16_bits_to_f32(mx.gemm_f16_ref(bits16(a[rows]), bits16(b_t), "bf16"))
+    assert_close(as_f32(c[rows]), ref, TOL_F16, ref_atol=False)
+    full = a.float() @ b_t.float().T
+    assert ((c.float() - full).abs().max() / full.abs().max()).item() <= TOL_F16
+
+
+def test_a4w4_cfg4_shard_sampled_blocks(cuda_device):
+    """Config 4 at 8 GPUs: one rank's shard, 16384 x 6656 x 16384 MXFP4 from
+    quantised N(0,1) data; eight seeded 128 x 128 blocks of C against the
+    oracle's dequantise-then-matmul on just the rows and columns they need."""
+    M, N, K = 16384, 53248 // 8, 16384
+    g = torch.Generator(device="cuda").manual_seed(404)
+    qa, sa = ops.quantize_mxfp4(torch.randn((M, K), generator=g, device="cuda"))
+    qb, sb = ops.quantize_mxfp4(torch.randn((N, K), generator=g, device="cuda"))
+    torch.cuda.empty_cache()
+    c = a4w4.matmul(qa, qb, sa, sb)
+    ops.check_status()
+    pick = torch.Generator().manual_seed(405)
+    for _ in range(8):
+        r0 = int(torch.randint(0, M // 128, (1,), generator=pick)) * 128
+        c0 = int(torch.randint(0, N // 128, (1,), generator=pick)) * 128
+        ref = mx.gemm_mxfp4_ref(qa[r0:r0 + 128].cpu().numpy(), qb[c0:c0 + 128].cpu().numpy(),
+                                sa[r0:r0 + 128].cpu().numpy(), sb[c0:c0 + 128].cpu().numpy())
+        got = bits16(c[r0:r0 + 128, c0:c0 + 128])
+        assert_close(mx.bf16_bits_to_f32(got), mx.bf16_bits_to_f32(ref), TOL_F8, ref_atol=False)
+
+
 E5M2_SHAPES = [(128, 256, 128), (256, 512, 1024), (300, 700, 208), (1000, 1000, 2048)]
 
 
