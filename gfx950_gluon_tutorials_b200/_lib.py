@@ -21,6 +21,7 @@ EINVAL, ESHAPE, EALIGN, ESTRIDE, EWORKSPACE, ETENSORMAP, ENODEVICE, ECAPACITY = 
     -1, -2, -3, -4, -5, -6, -7, -8)
 STATUS_TIMEOUT = 0x1000
 STATUS_SMEM_BASE = 0x2000
+STATUS_BAD_GROUPS = 0x3000
 SITE_EMPTY, SITE_FULL, SITE_ACC_EMPTY, SITE_ACC_FULL, SITE_OVERLAP, SITE_FLAG = 1, 2, 3, 4, 5, 6
 SITE_SCALES = 7
 OPT_PAIR, OPT_SK_MODE, OPT_GROUP_M, OPT_MIN_SK_ITERS, OPT_TIMEOUT_MS = 1, 2, 3, 4, 5
@@ -44,6 +45,10 @@ SIGNATURES = {
     "b2g_gemm_mxf4": (_c_int, [_vp, _c_i64, _vp, _c_i64, _vp, _c_i64, _c_i64, _vp, _c_i64,
                                _c_i64, _vp, _c_i64, _c_int, _c_int, _c_int, _c_int, _vp, _c_sz,
                                _vp, _vp]),
+    "b2g_gemm_mxf4_grouped": (_c_int, [_vp, _c_i64, _vp, _c_i64, _vp, _c_i64, _c_i64, _vp,
+                                       _c_i64, _c_i64, _vp, _c_i64, _vp, _c_int, _c_int, _c_int,
+                                       _c_int, _c_int, _vp, _c_sz, _vp, _vp]),
+    "b2g_gemm_grouped_workspace_bytes": (_c_sz, [_c_int, _c_int, _c_int, _c_int]),
     "b2g_gemm_mxf4_noalloc": (_c_int, [_vp, _c_i64, _vp, _c_i64, _vp, _c_i64, _c_i64, _vp,
                                        _c_i64, _c_i64, _vp, _c_i64, _c_int, _c_int, _c_int,
                                        _c_int, _vp, _vp]),

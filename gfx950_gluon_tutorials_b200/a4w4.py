@@ -12,6 +12,7 @@ from __future__ import annotations
 
 import torch
 
+from . import ops
 from .ops import gemm_mxf4
 
 BLOCK_M, BLOCK_N, BLOCK_K = 128, 256, 256
@@ -27,3 +28,12 @@ def matmul(a: torch.Tensor, b: torch.Tensor, a_scales: torch.Tensor,
 def matmul_kernel_only(a: torch.Tensor, b: torch.Tensor, a_scales: torch.Tensor,
                        b_scales: torch.Tensor, c: torch.Tensor) -> torch.Tensor:
     return gemm_mxf4(a, b, a_scales, b_scales, c)
+
+
+def grouped_matmul(a: torch.Tensor, b_experts: torch.Tensor, a_scales: torch.Tensor,
+                   b_scales, group_offsets: torch.Tensor,
+                   c: torch.Tensor | None = None) -> torch.Tensor:
+    """MoE grouped MXFP4 GEMM (the reference's roadmap item "4-bit MoE kernel",
+    ROADMAP.md): rows [g[e], g[e+1]) of `a` are multiplied by expert e's
+    weights b_experts[e]; see ops.gemm_mxf4_grouped for the layout rules."""
+    return ops.gemm_mxf4_grouped(a, b_experts, a_scales, b_scales, group_offsets, c=c)

@@ -151,7 +151,9 @@ int64_t blocked_scale_bytes(int64_t rows, int64_t K) {
 }
 
 // `pair_cap`: how many CTA pairs the device can hold at once (0 = sms / 2).
-Geometry geometry(int kind, int M, int N, int K, int sms, int pair_cap = 0) {
+// `b_rows`: rows of B and its scales (N, or groups * N for a grouped GEMM).
+Geometry geometry(int kind, int M, int N, int K, int sms, int pair_cap = 0, int b_rows = 0) {
+  if (b_rows <= 0) b_rows = N;
   Geometry g{};
   g.cg = g_opt.pair.load() != 0 ? 2 : 1;
   int units = g.cg == 2 ? sms / 2 : sms;
@@ -185,7 +187,7 @@ Geometry geometry(int kind, int M, int N, int K, int sms, int pair_cap = 0) {
   g.sfa_bytes = is_scaled(kind) ? static_cast<size_t>(blocked_scale_bytes(M, K)) : 0;
   off += align256(g.sfa_bytes);
   g.sfb_off = off;
-  g.sfb_bytes = is_scaled(kind) ? static_cast<size_t>(blocked_scale_bytes(N, K)) : 0;
+  g.sfb_bytes = is_scaled(kind) ? static_cast<size_t>(blocked_scale_bytes(b_rows, K)) : 0;
   off += align256(g.sfb_bytes);
   g.total = off;
   return g;
@@ -367,6 +369,8 @@ struct GemmCall {
   size_t ws_bytes;
   int* status;
   cudaStream_t stream;
+  const int32_t* groups;  // grouped GEMM: device row offsets (n_groups + 1), else null
+  int n_groups;
 };
 
 // Storage bytes per stored element of A/B (packed e2m1: one byte holds 2).
@@ -393,6 +397,10 @@ int check_call(const GemmCall& c) {
     return B2G_ESTRIDE;
   if (is_scaled(c.kind) && ((c.sfa_s0 == 0) != (c.sfa_s1 == 0) || (c.sfb_s0 == 0) != (c.sfb_s1 == 0)))
     return B2G_ESTRIDE;
+  if (c.groups != nullptr) {
+    if (c.kind != B2G_KIND_MXFP4 || c.n_groups < 1) return B2G_EINVAL;
+    if (c.N % 128 != 0 || static_cast<int64_t>(c.n_groups) * c.N > (1 << 30)) return B2G_ESHAPE;
+  }
   return B2G_OK;
 }
 
@@ -439,8 +447,9 @@ int run_gemm(const GemmCall& c) {
   cudaGetDevice(&dev);
   const int sms = current_sms();
   if (sms <= 0) return B2G_ENODEVICE;
-  if (use_skinny(c.kind, c.M)) return run_skinny(c, sms);
-  const Geometry g = geometry(c.kind, c.M, c.N, c.K, sms, pair_capacity(dev, sms));
+  if (c.groups == nullptr && use_skinny(c.kind, c.M)) return run_skinny(c, sms);
+  const int b_rows = c.groups != nullptr ? c.n_groups * c.N : c.N;
+  const Geometry g = geometry(c.kind, c.M, c.N, c.K, sms, pair_capacity(dev, sms), b_rows);
   if (g.total > 0 && (c.ws == nullptr || c.ws_bytes < g.total)) return B2G_EWORKSPACE;
   if (c.ws != nullptr && (reinterpret_cast<uintptr_t>(c.ws) & 255u) != 0) return B2G_EALIGN;
   uint8_t* ws = static_cast<uint8_t*>(c.ws);
@@ -453,7 +462,7 @@ int run_gemm(const GemmCall& c) {
   rc = encode_2d(&prm.tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, c.A, rb, static_cast<uint64_t>(c.M),
                  static_cast<uint64_t>(c.lda * eb), 128, 128, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc != B2G_OK) return rc;
-  rc = encode_2d(&prm.tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, c.B, rb, static_cast<uint64_t>(c.N),
+  rc = encode_2d(&prm.tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, c.B, rb, static_cast<uint64_t>(b_rows),
                  static_cast<uint64_t>(c.ldb * eb), 128, g.cg == 1 ? 256 : 128,
                  CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc != B2G_OK) return rc;
@@ -473,7 +482,7 @@ int run_gemm(const GemmCall& c) {
       relayout = true;
       const cudaError_t e = launch_sf_relayout(
           a_blocked ? nullptr : c.sfa, c.sfa_s0, c.sfa_s1, c.M, ws + g.sfa_off,
-          b_blocked ? nullptr : c.sfb, c.sfb_s0, c.sfb_s1, c.N, ws + g.sfb_off, c.K / 32,
+          b_blocked ? nullptr : c.sfb, c.sfb_s0, c.sfb_s1, b_rows, ws + g.sfb_off, c.K / 32,
           c.stream);
       if (e != cudaSuccess) return static_cast<int>(e);
     }
@@ -484,7 +493,7 @@ int run_gemm(const GemmCall& c) {
                    CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc != B2G_OK) return rc;
     rc = encode_2d(&prm.tmSFB, CU_TENSOR_MAP_DATA_TYPE_UINT32, sfb, row_words,
-                   static_cast<uint64_t>((c.N + 127) / 128), row_words * 4, gwords, 2,
+                   static_cast<uint64_t>((b_rows + 127) / 128), row_words * 4, gwords, 2,
                    CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc != B2G_OK) return rc;
   }
@@ -503,7 +512,10 @@ int run_gemm(const GemmCall& c) {
   prm.N = c.N;
   prm.K = c.K;
   prm.inject = static_cast<int32_t>(g_opt.inject.load());
-  prm.prefetch = static_cast<int32_t>(g_opt.prefetch.load());
+  prm.prefetch = c.groups != nullptr ? 0 : static_cast<int32_t>(g_opt.prefetch.load());
+  prm.groups = c.groups;
+  prm.n_groups = c.n_groups;
+  prm.group_rows = c.N;
   prm.timeout_ns = static_cast<uint64_t>(g_opt.timeout_ms.load()) * 1000000ull;
   prm.k_chunks = static_cast<int32_t>((rb + 127) / 128);
   return dispatch(c.kind, g.cg, prm, g.launched, c.out_dtype, relayout, c.stream);
@@ -573,6 +585,9 @@ const char* b2g_strerror(int code) {
     case B2G_ETENSORMAP: return "TMA descriptor rejected by the driver";
     case B2G_ENODEVICE: return "no sm_100 device is current";
     case B2G_ECAPACITY: return "size exceeds the entry point's fixed capacity";
+    case B2G_STATUS_BAD_GROUPS:
+      return "grouped GEMM refused to run: group offsets must start at 0, end at M, not "
+             "decrease and be multiples of the tile height";
     case B2G_STATUS_SMEM_BASE:
       return "kernel refused to run: dynamic shared memory base needs more alignment padding "
              "than was reserved";
@@ -641,6 +656,35 @@ int b2g_gemm_mxf4(const uint8_t* A, int64_t lda, const uint8_t* B, int64_t ldb,
   c.ws = workspace; c.ws_bytes = workspace_bytes; c.status = status;
   c.stream = static_cast<cudaStream_t>(stream);
   return run_gemm(c);
+}
+
+int b2g_gemm_mxf4_grouped(const uint8_t* A, int64_t lda, const uint8_t* B, int64_t ldb,
+                          const uint8_t* sfa, int64_t sfa_s0, int64_t sfa_s1, const uint8_t* sfb,
+                          int64_t sfb_s0, int64_t sfb_s1, void* C, int64_t ldc,
+                          const int32_t* group_offsets, int groups, int M, int N, int K,
+                          int out_dtype, void* workspace, size_t workspace_bytes, int* status,
+                          void* stream) {
+  if (group_offsets == nullptr || groups < 1) return B2G_EINVAL;
+  GemmCall c{};
+  c.kind = B2G_KIND_MXFP4;
+  c.A = A; c.lda = lda; c.B = B; c.ldb = ldb;
+  c.sfa = sfa; c.sfa_s0 = sfa_s0; c.sfa_s1 = sfa_s1;
+  c.sfb = sfb; c.sfb_s0 = sfb_s0; c.sfb_s1 = sfb_s1;
+  c.C = C; c.ldc = ldc; c.M = M; c.N = N; c.K = K; c.out_dtype = out_dtype;
+  c.ws = workspace; c.ws_bytes = workspace_bytes; c.status = status;
+  c.stream = static_cast<cudaStream_t>(stream);
+  c.groups = group_offsets;
+  c.n_groups = groups;
+  return run_gemm(c);
+}
+
+size_t b2g_gemm_grouped_workspace_bytes(int M, int N, int K, int groups) {
+  if (M < 1 || N < 1 || K < 1 || groups < 1) return 0;
+  int dev = -1;
+  cudaGetDevice(&dev);
+  const int sms = current_sms();
+  if (sms <= 0) return 0;
+  return geometry(B2G_KIND_MXFP4, M, N, K, sms, pair_capacity(dev, sms), groups * N).total;
 }
 
 int b2g_quant_mxfp4(const float* src, int64_t ld, int rows, int K, uint8_t* q, int64_t ldq,

@@ -75,6 +75,12 @@ struct alignas(64) GemmParams {
   int32_t prefetch;     // k-iterations the producer pulls into L2 ahead of its loads
   int32_t has_tmp;      // tmP is valid
   int32_t k_chunks;     // 128-byte K chunks per row (the last stage may hold fewer)
+  // Grouped GEMM (MoE experts): rows [groups[e], groups[e+1]) of A and C use
+  // rows [e * group_rows, (e + 1) * group_rows) of B (and its scales). Null
+  // for a plain GEMM.
+  const int32_t* groups;
+  int32_t n_groups;
+  int32_t group_rows;
   uint64_t timeout_ns;
 };
 
@@ -233,6 +239,20 @@ __device__ __noinline__ bool wait_flag(const uint32_t* flag, uint32_t want,
   }
 }
 
+// Grouped GEMM: the group whose rows [groups[e], groups[e+1]) contain `row`
+// (the last of equal offsets, so empty groups are skipped).
+__device__ __forceinline__ int32_t expert_of(const GemmParams& p, int32_t row) {
+  int32_t lo = 0, hi = p.n_groups - 1;
+  while (lo < hi) {
+    const int32_t mid = (lo + hi + 1) >> 1;
+    if (__ldg(p.groups + mid) <= row)
+      lo = mid;
+    else
+      hi = mid - 1;
+  }
+  return lo;
+}
+
 template <bool kBF16>
 __device__ __forceinline__ uint32_t pack_out(uint32_t lo, uint32_t hi) {
   const float a = __uint_as_float(lo), b = __uint_as_float(hi);
@@ -267,6 +287,31 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
     // the same for every CTA of the launch: nothing has been touched yet
     if (threadIdx.x == 0) report_status(p, B2G_STATUS_SMEM_BASE);
     return;
+  }
+  if (p.groups != nullptr) {
+    // Group offsets are read from device memory: every CTA checks them the
+    // same way (0 first, M last, non-decreasing, multiples of the tile
+    // height) and, if they are not, returns before touching anything.
+    // a word of the misc area (tmem slot, abort flag, this) not yet in use
+    volatile uint32_t& groups_ok = *reinterpret_cast<volatile uint32_t*>(smem + SP::kMiscOff + 8);
+    if (threadIdx.x < 32) {
+      bool ok = true;
+      for (int32_t e = static_cast<int32_t>(threadIdx.x); e <= p.n_groups; e += 32) {
+        const int32_t o = __ldg(p.groups + e);
+        ok = ok && o >= 0 && o <= p.M && (o % (128 * CG)) == 0;
+        if (e > 0) ok = ok && __ldg(p.groups + e - 1) <= o;
+      }
+      ok = __all_sync(0xffffffffu, ok);
+      if (threadIdx.x == 0) {
+        ok = ok && __ldg(p.groups) == 0 && __ldg(p.groups + p.n_groups) == p.M;
+        groups_ok = ok ? 1u : 0u;
+      }
+    }
+    __syncthreads();
+    if (groups_ok == 0u) {
+      if (threadIdx.x == 0) report_status(p, B2G_STATUS_BAD_GROUPS);
+      return;
+    }
   }
   const uint32_t sbase = smem_u32(smem);
   const uint32_t warp = threadIdx.x >> 5;
@@ -353,7 +398,10 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
       for (int32_t i = 0; i < p.prefetch; ++i) prefetch_one();
       while (alive && cursor_next(p.plan, unit, cur, w)) {
         const int32_t a_row = w.tm * (128 * CG) + static_cast<int32_t>(rank) * 128;
-        const int32_t b_row = w.tn * 256 + (CG == 2 ? static_cast<int32_t>(rank) * 128 : 0);
+        // grouped GEMM: the expert whose rows hold this M-tile picks B's rows
+        const int32_t b_base = p.groups != nullptr ? expert_of(p, w.tm * (128 * CG)) * p.group_rows : 0;
+        const int32_t b_row =
+            b_base + w.tn * 256 + (CG == 2 ? static_cast<int32_t>(rank) * 128 : 0);
         for (int32_t k = w.k_begin; k < w.k_end; ++k, ++it) {
           const uint32_t s = it % STAGES, ph = (it / STAGES) & 1u;
           if (p.prefetch > 0) prefetch_one();
@@ -389,10 +437,10 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
               const int32_t sx = kc * kGps * 128;
               if constexpr (CG == 1) {
                 tma_load_2d(sfa_dst, &p.tmSFA, fb, sx, a_row >> 7);
-                tma_load_2d(sfb_dst, &p.tmSFB, fb, sx, w.tn * 2);
+                tma_load_2d(sfb_dst, &p.tmSFB, fb, sx, (b_base >> 7) + w.tn * 2);
               } else {
                 tma_load_2d_pair(sfa_dst, &p.tmSFA, fb, sx, a_row >> 7);
-                tma_load_2d_pair(sfb_dst, &p.tmSFB, fb, sx, w.tn * 2);
+                tma_load_2d_pair(sfb_dst, &p.tmSFB, fb, sx, (b_base >> 7) + w.tn * 2);
               }
             }
           }

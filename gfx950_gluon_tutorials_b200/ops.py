@@ -260,6 +260,50 @@ def gemm_mxf4(a: torch.Tensor, b_t: torch.Tensor, a_scales: torch.Tensor,
     return c
 
 
+def gemm_mxf4_grouped(a: torch.Tensor, b_experts: torch.Tensor, a_scales: torch.Tensor,
+                      b_scales, group_offsets: torch.Tensor, c: torch.Tensor | None = None,
+                      out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """MoE grouped a4w4: rows [g[e], g[e+1]) of A and C use expert e's weights.
+
+    a (M, K/2) packed e2m1, tokens sorted by expert with each expert's segment
+    padded to a multiple of 256 rows (128 with the pair option off);
+    b_experts (E, N, K/2) or (E * N, K/2); scales (M, K/32) and (E * N, K/32)
+    of any strides (or BlockedScales for the experts); group_offsets an int32
+    CUDA tensor of E + 1 row offsets (0 first, M last). Returns C (M, N)."""
+    dev = _require_cuda(a, b_experts, group_offsets)
+    if a.dtype != torch.uint8 or b_experts.dtype != torch.uint8:
+        raise ValueError("a4w4 operands are packed uint8")
+    if group_offsets.dtype != torch.int32 or group_offsets.dim() != 1:
+        raise ValueError("group_offsets must be a 1-D int32 tensor")
+    E = group_offsets.numel() - 1
+    if E < 1:
+        raise ValueError("need at least one group")
+    M, Kp = a.shape
+    if b_experts.dim() == 3:
+        if b_experts.shape[0] != E:
+            raise ValueError("b_experts has a different expert count than group_offsets")
+        b_experts = b_experts.reshape(-1, b_experts.shape[-1])
+    rows_b, Kp2 = b_experts.shape
+    if Kp != Kp2 or rows_b % E != 0:
+        raise ValueError("Incompatible dimensions")
+    N, K = rows_b // E, 2 * Kp
+    sa = _scale_args(a_scales, M, K, "a_scales")
+    sb = _scale_args(b_scales, rows_b, K, "b_scales")
+    c = _out(c, M, N, c.dtype if c is not None else out_dtype, dev)
+    a_, b_ = _k_major(a), _k_major(b_experts)
+    offs = group_offsets.contiguous()
+    cv, copy_back = _c_view(c)
+    ws = workspace(lib().b2g_gemm_grouped_workspace_bytes(M, N, K, E), dev)
+    rc = lib().b2g_gemm_mxf4_grouped(
+        a_.data_ptr(), a_.stride(0), b_.data_ptr(), b_.stride(0), *sa, *sb,
+        cv.data_ptr(), cv.stride(0), offs.data_ptr(), E, M, N, K, _OUT_DT[c.dtype],
+        ws.data_ptr(), ws.numel(), status_tensor(dev).data_ptr(), _stream_handle(dev))
+    check(rc, "b2g_gemm_mxf4_grouped")
+    if copy_back:
+        c.copy_(cv)
+    return c
+
+
 # ------------------------------------------------------------------ packing --
 def quantize_mxfp4(x: torch.Tensor, rows_pad: int | None = None
                    ) -> tuple[torch.Tensor, torch.Tensor]:

@@ -84,6 +84,7 @@ extern "C" {
 #define B2G_SITE_FLAG 6           /* stream-K owner waiting for a contributor */
 #define B2G_SITE_SCALES 7         /* MMA waiting for scale factors copied into TMEM */
 #define B2G_STATUS_SMEM_BASE 0x2000 /* kernel returned at entry: shared memory base misaligned */
+#define B2G_STATUS_BAD_GROUPS 0x3000 /* grouped GEMM returned at entry: group offsets invalid */
 
 /* Library ABI version (major * 100 + minor). */
 B2G_API int b2g_version(void);
@@ -157,6 +158,25 @@ B2G_API int b2g_gemm_mxf4_noalloc(const uint8_t* A, int64_t lda, const uint8_t* 
                                   const uint8_t* sfb, int64_t sfb_s0, int64_t sfb_s1, void* C,
                                   int64_t ldc, int M, int N, int K, int out_dtype, int* status,
                                   void* stream);
+
+/* MoE grouped a4w4: rows [g[e], g[e+1]) of A and C belong to expert e and are
+ * multiplied by expert e's weights, rows [e * N, (e + 1) * N) of B (`groups`
+ * experts stacked, (groups * N) x K/2 packed bytes, scales (groups * N, K/32)).
+ * `group_offsets` is a DEVICE array of groups + 1 int32: g[0] = 0,
+ * g[groups] = M, non-decreasing, every entry a multiple of the tile height
+ * (256 rows; 128 with B2G_OPT_PAIR = 0) - tokens sorted by expert with each
+ * expert's segment padded (padding rows of C are written with the products of
+ * whatever A holds there). Empty experts are allowed. N must be a multiple of
+ * 128. Offsets that break these rules set B2G_STATUS_BAD_GROUPS and nothing is
+ * written. Workspace: b2g_gemm_grouped_workspace_bytes. The reference has no
+ * MoE kernel yet (its roadmap plans a 4-bit MoE GEMM); this is that row. */
+B2G_API int b2g_gemm_mxf4_grouped(const uint8_t* A, int64_t lda, const uint8_t* B, int64_t ldb,
+                                  const uint8_t* sfa, int64_t sfa_s0, int64_t sfa_s1,
+                                  const uint8_t* sfb, int64_t sfb_s0, int64_t sfb_s1, void* C,
+                                  int64_t ldc, const int32_t* group_offsets, int groups, int M,
+                                  int N, int K, int out_dtype, void* workspace,
+                                  size_t workspace_bytes, int* status, void* stream);
+B2G_API size_t b2g_gemm_grouped_workspace_bytes(int M, int N, int K, int groups);
 
 /* Blocked E8M0 scale layout: for each 128-row block and each group of 4
  * k-blocks (4 scales), 512 bytes in which byte r0*16 + r1*4 + j holds the

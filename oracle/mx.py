@@ -174,6 +174,24 @@ def gemm_mxfp4_ref(a_fp4, b_fp4, a_scales, b_scales) -> np.ndarray:
     return f32_to_bf16_bits(a @ b.T)
 
 
+def gemm_mxfp4_grouped_ref(a_fp4, b_fp4, a_scales, b_scales, offsets) -> np.ndarray:
+    """Grouped a4w4 (MoE experts): gemm_mxfp4_ref per expert e on rows
+    [offsets[e], offsets[e+1]) of A with rows [e*N, (e+1)*N) of B, where
+    N = B rows / experts. No reference counterpart exists (its roadmap plans
+    the kernel); the per-group product is the reference's torch_reference.
+    Returns bf16 bits (M, N)."""
+    offsets = np.asarray(offsets)
+    E = len(offsets) - 1
+    N = b_fp4.shape[0] // E
+    out = np.zeros((a_fp4.shape[0], N), dtype=np.uint16)
+    for e in range(E):
+        r0, r1 = int(offsets[e]), int(offsets[e + 1])
+        if r1 > r0:
+            out[r0:r1] = gemm_mxfp4_ref(a_fp4[r0:r1], b_fp4[e * N:(e + 1) * N],
+                                        a_scales[r0:r1], b_scales[e * N:(e + 1) * N])
+    return out
+
+
 def gemm_mxe5m2_ref(a_q, b_q, a_scales, b_scales) -> np.ndarray:
     """Scaled BF8 in the same dequantise-then-fp32-mm pattern; bf16 bits."""
     a = e5m2_to_f32(a_q) * np.repeat(e8m0_to_f32(a_scales), SCALE_GROUP_SIZE, axis=1)

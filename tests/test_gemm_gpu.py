@@ -482,3 +482,73 @@ def test_flag_region_stays_zero_across_mixed_calls(cuda_device):
         if out is not None:
             c, ref = out
             assert_close(as_f32(c), ref.cpu().numpy(), TOL_F16, ref_atol=False)
+
+
+# --------------------------------------------------- MoE grouped MXFP4 GEMM
+def _grouped_inputs(sizes, N, K, seed, tile=256):
+    """Tokens sorted by expert, each expert's segment padded to `tile` rows;
+    reference-style random nibbles and E8M0 bytes 124..127, A scales
+    M-contiguous (the reference's storage)."""
+    g = torch.Generator().manual_seed(seed)
+    padded = [(s + tile - 1) // tile * tile for s in sizes]
+    offsets = np.concatenate([[0], np.cumsum(padded)]).astype(np.int32)
+    M, E = int(offsets[-1]), len(sizes)
+    a = torch.randint(0, 256, (M, K // 2), generator=g, dtype=torch.uint8)
+    b = torch.randint(0, 256, (E * N, K // 2), generator=g, dtype=torch.uint8)
+    sa = torch.randint(124, 128, (K // 32, M), generator=g, dtype=torch.uint8).T
+    sb = torch.randint(124, 128, (E * N, K // 32), generator=g, dtype=torch.uint8)
+    return a, b, sa, sb, offsets
+
+
+@pytest.mark.parametrize("sizes,N,K", [([300, 0, 512, 40], 512, 1024), ([256] * 8, 256, 512),
+                                       ([1000, 17], 384, 2048), ([0, 0, 600], 1024, 768)],
+                         ids=["ragged", "uniform8", "two", "leading_empty"])
+@pytest.mark.parametrize("pair", [1, 0])
+def test_grouped_mxfp4_matches_oracle(cuda_device, sizes, N, K, pair):
+    tile = 256 if pair else 128
+    a, b, sa, sb, offsets = _grouped_inputs(sizes, N, K, sum(sizes) + N + K, tile)
+    ref = mx.gemm_mxfp4_grouped_ref(a.numpy(), b.numpy(), sa.numpy(), sb.numpy(), offsets)
+    old = _lib.get_option(_lib.OPT_PAIR)
+    try:
+        _lib.set_option(_lib.OPT_PAIR, pair)
+        c = a4w4.grouped_matmul(a.cuda(), b.cuda(), sa.cuda(), sb.cuda(),
+                                torch.from_numpy(offsets).cuda())
+        ops.check_status()
+    finally:
+        _lib.set_option(_lib.OPT_PAIR, old)
+    got = bits16(c)
+    assert_close(mx.bf16_bits_to_f32(got), mx.bf16_bits_to_f32(ref), TOL_F8)
+    print(f"grouped {sizes}: bit-exact fraction {float(np.mean(got == ref)):.6f}")
+
+
+def test_grouped_mxfp4_preblocked_expert_scales_and_3d_weights(cuda_device):
+    """Static expert weights: scales relaid once (BlockedScales) and weights
+    passed as (E, N, K/2) give the same C as the per-call path."""
+    a, b, sa, sb, offsets = _grouped_inputs([512, 256, 768], 256, 1024, 77)
+    offs = torch.from_numpy(offsets).cuda()
+    E = len(offsets) - 1
+    c1 = a4w4.grouped_matmul(a.cuda(), b.cuda(), sa.cuda(), sb.cuda(), offs)
+    sb_blocked = ops.block_scales(sb.cuda(), 1024)
+    c2 = a4w4.grouped_matmul(a.cuda(), b.cuda().view(E, 256, -1), sa.cuda(), sb_blocked, offs)
+    ops.check_status()
+    assert torch.equal(c1, c2)
+
+
+def test_grouped_mxfp4_rejects_bad_offsets(cuda_device):
+    """Offsets that are not multiples of the tile height: status code, nothing
+    written; the next valid call works."""
+    a, b, sa, sb, offsets = _grouped_inputs([256, 256], 256, 512, 5)
+    bad = offsets.copy()
+    bad[1] = 200
+    c = torch.full((int(offsets[-1]), 256), 7.0, dtype=torch.bfloat16, device="cuda")
+    a4w4.grouped_matmul(a.cuda(), b.cuda(), sa.cuda(), sb.cuda(), torch.from_numpy(bad).cuda(),
+                        c=c)
+    with pytest.raises(_lib.B2GError) as info:
+        ops.check_status()
+    assert info.value.code == _lib.STATUS_BAD_GROUPS
+    assert bool((c == 7.0).all())
+    c_ok = a4w4.grouped_matmul(a.cuda(), b.cuda(), sa.cuda(), sb.cuda(),
+                               torch.from_numpy(offsets).cuda())
+    ops.check_status()
+    ref = mx.gemm_mxfp4_grouped_ref(a.numpy(), b.numpy(), sa.numpy(), sb.numpy(), offsets)
+    assert_close(as_f32(c_ok), mx.bf16_bits_to_f32(ref), TOL_F8)
