@@ -369,6 +369,41 @@ def time_skinny(world: int, peaks: dict, peak_src: str, iters: int = 20) -> dict
     return out
 
 
+def time_moe(world: int, peaks: dict, steps: int, warmup: int) -> dict:
+    """MoE grouped MXFP4 leg: 8 experts with 1024 tokens routed to each (an
+    8192-row A, tokens sorted by expert), expert weights N = 4096 x K = 8192,
+    quantised N(0,1) data, expert scales relaid once (static weights)."""
+    from gfx950_gluon_tutorials_b200 import a4w4, ops
+    E, rows, N, K = 8, 1024, 4096, 8192
+    dev = torch.device("cuda", torch.cuda.current_device())
+    gen = torch.Generator(device=dev).manual_seed(91)
+    qa, sa = ops.quantize_mxfp4(torch.randn((E * rows, K), generator=gen, device=dev))
+    qb, sb = ops.quantize_mxfp4(torch.randn((E * N, K), generator=gen, device=dev))
+    sb = ops.block_scales(sb, K)
+    offs = torch.arange(0, E * rows + 1, rows, dtype=torch.int32, device=dev)
+    c = torch.empty((E * rows, N), dtype=torch.bfloat16, device=dev)
+    for _ in range(warmup):
+        a4w4.grouped_matmul(qa, qb, sa, sb, offs, c=c)
+    barrier(world)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        a4w4.grouped_matmul(qa, qb, sa, sb, offs, c=c)
+    end.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(start.elapsed_time(end) / steps, world)
+    ops.check_status()
+    flops = 2.0 * E * rows * N * K
+    tf = flops / (ms * 1e-3) / 1e12
+    del qa, qb, sa, sb, c
+    torch.cuda.empty_cache()
+    return {"workload": f"{E} experts x {rows} tokens, N={N} K={K} MXFP4 per GPU",
+            "ms_per_step": ms, "tflops_per_gpu": tf,
+            "frac_of_measured": tf / tensor_peak("mxfp4", peaks),
+            "launches_per_step": 2}
+
+
 def time_allgather(w: Workload, world: int, iters: int = 10) -> dict | None:
     """Separately timed NCCL all-gather of every rank's C slab into a
     [world][M][N/world] buffer in each GPU's own memory."""
@@ -469,6 +504,8 @@ def contract_main(args):
     gather = time_allgather(w, world)
     skinny = None if args.no_extra or args.config == "large" else time_skinny(world, peaks,
                                                                                peak_src)
+    moe = None if args.no_extra or args.config == "large" else time_moe(
+        world, peaks, args.steps, args.warmup)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_reference_tflops(M, n_local, K, args.cpu_budget, os.cpu_count() or 1)
@@ -523,6 +560,8 @@ def contract_main(args):
             line["allgather"] = gather
         if skinny is not None:
             line["skinny"] = skinny
+        if moe is not None:
+            line["moe_grouped_mxfp4"] = moe
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()
