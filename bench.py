@@ -423,8 +423,48 @@ def time_allgather(w: Workload, world: int, iters: int = 10) -> dict | None:
     torch.cuda.synchronize()
     ms = max_over_ranks(start.elapsed_time(end) / iters, world)
     total = out.numel() * out.element_size()
-    return {"bytes": total, "ms": ms, "algbw_gbs": total / ms / 1e6,
-            "busbw_gbs": total * (world - 1) / world / ms / 1e6}
+    res = {"bytes": total, "ms": ms, "algbw_gbs": total / ms / 1e6,
+           "busbw_gbs": total * (world - 1) / world / ms / 1e6}
+    if w.dtype_name in ("fp16", "bf16"):
+        res.update(time_gemm_gather(w, world, iters))
+    return res
+
+
+def time_gemm_gather(w: Workload, world: int, iters: int, chunks: int = 4) -> dict:
+    """The slab GEMM followed by the gather of C, as one step: sequential
+    (GEMM, then the NCCL all-gather) against `shard.gemm_gather_p2p` (row
+    chunks written into a symmetric buffer, each chunk copied to the peers by
+    the copy engines while the next chunk computes)."""
+    from gfx950_gluon_tutorials_b200.shard import gather_slabs, gemm_gather_p2p
+    ops = w.ops
+    s = w.sets[0]
+    copy = torch.cuda.Stream()
+
+    def sequential():
+        return gather_slabs(ops.gemm_f16(s["a"], s["b"], s["c"]))
+
+    def overlapped():
+        return gemm_gather_p2p(lambda x, y, out: ops.gemm_f16(x, y, out), s["a"], s["b"],
+                               chunks=chunks, out_dtype=s["c"].dtype, copy_stream=copy)
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        barrier(world)
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(iters):
+            fn()
+        end.record()
+        torch.cuda.synchronize()
+        return max_over_ranks(start.elapsed_time(end) / iters, world)
+
+    seq = timed(sequential)
+    ovl = timed(overlapped)
+    ops.check_status()
+    return {"gemm_then_gather_ms": seq, "gemm_gather_p2p_overlapped_ms": ovl,
+            "overlap_chunks": chunks}
 
 
 def cpu_reference_tflops(M: int, N: int, K: int, budget_s: float, threads: int) -> dict:

@@ -5,11 +5,18 @@ computes its slab of C with no collective in the loop. An optional NCCL
 all-gather then lands every slab in every GPU's own memory as a [world][M][n]
 buffer (`gather_slabs`), and `assemble` permutes it to row-major M x N.
 
+`gemm_gather_p2p` runs the slab GEMM in row chunks and copies each finished
+chunk into every peer's symmetric buffer on a second stream (copy engines over
+NVLink) while the next chunk computes, so the transfer of C hides behind the
+tensor-core work.
+
 The reference has no multi-GPU code; this follows the build target's plan for
 its large MXFP4 configuration (16384 x 53248 x 16384 split over 2, 4, 8 GPUs).
 """
 
 from __future__ import annotations
+
+from collections.abc import Callable
 
 import torch
 
@@ -41,3 +48,67 @@ def assemble(slabs: torch.Tensor) -> torch.Tensor:
     """[world][M][n] -> M x (world * n) row-major (rank r owns columns r*n ..)."""
     world, m, n = slabs.shape
     return slabs.permute(1, 0, 2).reshape(m, world * n)
+
+
+def chunk_rows(m: int, chunks: int, align: int = 256) -> list[tuple[int, int]]:
+    """[start, stop) row ranges splitting m rows into about `chunks` pieces of
+    whole `align`-row tiles (fewer pieces when m has fewer tiles)."""
+    tiles = -(-m // align)
+    chunks = max(1, min(chunks, tiles))
+    out = []
+    for i in range(chunks):
+        lo = (tiles * i // chunks) * align
+        hi = min(m, (tiles * (i + 1) // chunks) * align)
+        if hi > lo:
+            out.append((lo, hi))
+    return out
+
+
+_SYMM: dict = {}
+
+
+def gemm_gather_p2p(matmul: Callable[..., torch.Tensor], a: torch.Tensor,
+                    b_shard: torch.Tensor, chunks: int = 4, group=None,
+                    out_dtype: torch.dtype = torch.float16,
+                    copy_stream: "torch.cuda.Stream | None" = None) -> torch.Tensor:
+    """Every rank's slab C_r = A @ B_r^T, gathered into [world][M][n] in every
+    GPU's memory, with the transfer overlapping the GEMM.
+
+    The gather buffer is symmetric memory: each row chunk's GEMM writes
+    straight into this rank's slot of its own buffer (`matmul(a_rows, b_shard,
+    out_view)` on the current stream); a second stream then copies the chunk
+    into every peer's buffer (peer-to-peer copies run on the copy engines over
+    NVLink and take no SMs from the persistent GEMM) while the next chunk
+    computes. A symmetric-memory barrier before the first write and after the
+    last copy orders the ranks. The buffer is reused by the next call with the
+    same shape: the result is valid until then. Every rank passes the same
+    shapes and chunk count."""
+    import torch.distributed._symmetric_memory as symm_mem
+    world = torch.distributed.get_world_size(group)
+    rank = torch.distributed.get_rank(group)
+    m, n = a.shape[0], b_shard.shape[0]
+    key = (m, n, out_dtype, a.device, id(group))
+    if key not in _SYMM:
+        buf = symm_mem.empty((world, m, n), dtype=out_dtype, device=a.device)
+        hdl = symm_mem.rendezvous(buf, group if group is not None
+                                  else torch.distributed.group.WORLD)
+        peers = [hdl.get_buffer(p, (world, m, n), out_dtype) for p in range(world)]
+        _SYMM[key] = (buf, hdl, peers)
+    buf, hdl, peers = _SYMM[key]
+    compute = torch.cuda.current_stream(a.device)
+    copy = copy_stream or torch.cuda.Stream(device=a.device)
+    hdl.barrier()  # every rank is done with the previous contents
+    copy.wait_stream(compute)
+    for lo, hi in chunk_rows(m, chunks):
+        mine = buf[rank, lo:hi]
+        matmul(a[lo:hi], b_shard, mine)
+        done = torch.cuda.Event()
+        done.record(compute)
+        copy.wait_event(done)
+        with torch.cuda.stream(copy):
+            for p in range(world):
+                if p != rank:
+                    peers[p][rank, lo:hi].copy_(mine, non_blocking=True)
+    compute.wait_stream(copy)
+    hdl.barrier()  # every rank's copies into this buffer have landed
+    return buf

@@ -12,7 +12,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from gfx950_gluon_tutorials_b200.shard import assemble, gather_slabs, shard_range
+from gfx950_gluon_tutorials_b200.shard import assemble, chunk_rows, gather_slabs, shard_range
 
 
 @pytest.mark.parametrize("n,world", [(4096, 1), (53248, 2), (53248, 8), (700, 3), (300, 4)])
@@ -90,3 +90,12 @@ def test_a_failing_rank_is_reported_not_hung():
     assert out.get(1, "").startswith("error: injected")
     # the surviving rank's collective ends with an error within the group timeout
     assert out.get(0, "").startswith("error")
+
+
+@pytest.mark.parametrize("m,chunks", [(4096, 4), (1000, 3), (256, 8), (16384, 5)])
+def test_chunk_rows_cover_whole_tiles(m, chunks):
+    pieces = chunk_rows(m, chunks)
+    assert pieces[0][0] == 0 and pieces[-1][1] == m
+    for (lo, hi), (lo2, _) in zip(pieces, pieces[1:]):
+        assert hi == lo2 and lo % 256 == 0
+    assert len(pieces) <= chunks
