@@ -404,6 +404,40 @@ def time_moe(world: int, peaks: dict, steps: int, warmup: int) -> dict:
             "launches_per_step": 2}
 
 
+def time_attention(world: int, peaks: dict, peak_src: str, steps: int, warmup: int) -> dict:
+    """Attention forward leg: the reference FMHA bench's default problem
+    (B=1, HQ=HK=64, S=8192, D=128, bf16, bhsd, non-causal) on every rank.
+    q, k and v together are 384 MB, above the 126 MB L2."""
+    from gfx950_gluon_tutorials_b200 import attention, ops
+    B, H, S, D = 1, 64, 8192, 128
+    dev = torch.device("cuda", torch.cuda.current_device())
+    q, k, v, md = attention.input_helper(B, H, H, S, S, D, torch.bfloat16, "bhsd", device=dev)
+    o = torch.empty_like(q)
+    for _ in range(max(3, warmup)):
+        attention.run_gluon_attention(q, k, v, o, md)
+    barrier(world)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        attention.run_gluon_attention(q, k, v, o, md)
+    end.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(start.elapsed_time(end) / steps, world)
+    ops.check_status()
+    flops = attention.compute_flops(B, H, S, S, D, False)
+    tf = flops / (ms * 1e-3) / 1e12
+    del q, k, v, o
+    torch.cuda.empty_cache()
+    return {"workload": f"FMHA forward B={B} HQ=HK={H} S={S} D={D} bf16 bhsd non-causal per GPU",
+            "ms_per_call": ms, "tflops_per_gpu": tf,
+            "roofline": {"bound": "tensor", "achieved": tf, "peak": peaks["bf16_tflops"],
+                         "unit": "TFLOP/s", "frac": tf / peaks["bf16_tflops"],
+                         "algorithmic_flops_per_launch": flops,
+                         "peak_source": f"{peak_src} bf16_tflops (burst)"},
+            "launches_per_call": 1}
+
+
 def time_allgather(w: Workload, world: int, iters: int = 10) -> dict | None:
     """Separately timed NCCL all-gather of every rank's C slab into a
     [world][M][N/world] buffer in each GPU's own memory."""
@@ -546,6 +580,8 @@ def contract_main(args):
                                                                                peak_src)
     moe = None if args.no_extra or args.config == "large" else time_moe(
         world, peaks, args.steps, args.warmup)
+    attn = None if args.no_extra or args.config == "large" else time_attention(
+        world, peaks, peak_src, args.steps, args.warmup)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_reference_tflops(M, n_local, K, args.cpu_budget, os.cpu_count() or 1)
@@ -602,6 +638,8 @@ def contract_main(args):
             line["skinny"] = skinny
         if moe is not None:
             line["moe_grouped_mxfp4"] = moe
+        if attn is not None:
+            line["attention_fwd"] = attn
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()

@@ -19,7 +19,7 @@ CSRC = os.path.join(PKG_DIR, "csrc")
 INCLUDE = os.path.join(REPO_DIR, "include")
 LIB_PATH = os.path.join(PKG_DIR, "libb2g.so")
 
-SOURCES = ["capi.cu", "pack.cu", "noalloc.cu"]
+SOURCES = ["capi.cu", "pack.cu", "noalloc.cu", "attention.cu"]
 HEADERS = ["ptx.cuh", "sched.h", "gemm_kernel.cuh", "skinny_kernel.cuh", "pack.cuh",
            "capi_internal.h"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -1,0 +1,543 @@
+// Flash-attention forward (non-causal, GQA) for sm_100a: O = softmax(Q K^T * s) V
+// and the row log-sum-exp, the reference's FMHA forward
+// (kernels/attention/fmha_v4.py:343-758, launcher :761-790; torch oracle
+// kernels/attention/common.py:115-138 sdpa_reference).
+//
+// One CTA per (128 query rows, query head, batch). Per KV tile of 128 keys:
+//   S_j  = Q K_j^T           tcgen05.mma into one of two TMEM score buffers
+//   P_j  = exp2(S_j*s' - m)  softmax warps, one query row per thread, P stored
+//                            back to TMEM as 16-bit values
+//   O   += P_j V_j           tcgen05.mma with A = P read from TMEM and B = V as an
+//                            MN-major shared-memory operand (no transpose pass)
+// The MMA thread issues S_{j+1} before PV_j, so the next score tile is computed
+// while the softmax of this one runs. The running max m is kept in log2 units
+// (s' = sm_scale * log2 e); when a row's max moves, its O row is rescaled in
+// TMEM by exp2(m_old - m_new) before PV_j accumulates.
+//
+// CTA layout (192 threads): warp 0 one-thread TMA producer (Q once; K and V
+// through two-stage rings), warp 1 one-thread MMA issuer (owns the 512 TMEM
+// columns), warps 2-5 softmax and epilogue (TMEM lane quarter w % 4). Q, K,
+// V and O are addressed through 4-D views (d, sequence, head, batch) built
+// from the caller's strides, so bhsd and bshd layouts and GQA (query head h
+// reads key/value head h / (HQ / HK)) need no copies; keys and query rows
+// past the sequence ends are zero-filled by TMA and masked.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+#include <type_traits>
+
+#include "b2g.h"
+#include "capi_internal.h"
+#include "ptx.cuh"
+
+namespace b2g {
+
+struct alignas(64) FmhaParams {
+  CUtensorMap tmQ, tmK, tmV;  // 4-D (d, seq, head, batch), 64 x 128 x 1 x 1 boxes, 128B swizzle
+  void* O;                    // output, same element type as Q
+  int64_t o_sb, o_sh, o_ss;   // element strides of O (d contiguous)
+  float* lse;                 // [B][HQ][S_q] natural-log log-sum-exp, or null
+  int* status;
+  int32_t HQ, HK, S_q, S_k;
+  float scale_log2;           // sm_scale * log2(e)
+  uint64_t timeout_ns;
+};
+
+template <int D>
+struct FmhaPlan {
+  static constexpr uint32_t kThreads = 192;
+  static constexpr uint32_t kRegions = D / 64;             // 64-element (128-byte) column slabs
+  static constexpr uint32_t kRegion = 128 * 128;           // 128 rows x 128 bytes
+  static constexpr uint32_t kTile = kRegions * kRegion;    // Q, one K or one V tile
+  static constexpr uint32_t kStages = 2;                   // K ring and V ring depth
+  static constexpr uint32_t kQOff = 0;
+  static constexpr uint32_t kKOff = kQOff + kTile;
+  static constexpr uint32_t kVOff = kKOff + kStages * kTile;
+  static constexpr uint32_t kBarOff = kVOff + kStages * kTile;
+  // q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], s_free[2],
+  // p_full[2], pv_done[2]
+  static constexpr uint32_t kNumBars = 1 + 4 * kStages + 8;
+  static constexpr uint32_t kMiscOff = kBarOff + kNumBars * 8;  // tmem slot, abort flag
+  static constexpr uint32_t kBytes = kMiscOff + 16;
+  static constexpr uint32_t kDynBytes = kBytes + 1024;  // + alignment slack
+  // TMEM columns: S0, S1 (128 fp32 each), O (D fp32), P0, P1 (64 x 2 x 16-bit each)
+  static constexpr uint32_t kS0 = 0, kS1 = 128, kO = 256, kP0 = 384, kP1 = 448;
+  static_assert(D == 64 || D == 128, "head dim");
+  static_assert(kDynBytes <= 232448, "shared memory");
+};
+
+template <int D, bool kBF16>
+__host__ __device__ constexpr uint32_t fmha_idesc_s() {
+  // D fp32 | A, B fmt | both K-major | N = 128 keys | M = 128 rows
+  constexpr uint32_t f = kBF16 ? 1u : 0u;
+  return (1u << 4) | (f << 7) | (f << 10) | ((128u >> 3) << 17) | ((128u >> 4) << 24);
+}
+
+template <int D, bool kBF16>
+__host__ __device__ constexpr uint32_t fmha_idesc_pv() {
+  // D fp32 | A, B fmt | A K-major (TMEM), B MN-major (V, d contiguous) | N = D | M = 128
+  constexpr uint32_t f = kBF16 ? 1u : 0u;
+  return (1u << 4) | (f << 7) | (f << 10) | (1u << 16) | ((static_cast<uint32_t>(D) >> 3) << 17) |
+         ((128u >> 4) << 24);
+}
+
+__device__ __forceinline__ void fmha_report(const FmhaParams& p, int code) {
+  if (p.status != nullptr) atomicCAS(p.status, 0, code);
+}
+
+// Bounded mbarrier wait: sleeping probes, then the deadline and the CTA's
+// abort flag between them.
+template <bool kClusterScope = false>
+__device__ __noinline__ bool fmha_wait_slow(uint32_t bar, uint32_t parity,
+                                            volatile uint32_t* abort_flag, const FmhaParams& p,
+                                            int site) {
+  const uint64_t t0 = globaltimer_ns();
+#pragma unroll 1
+  while (true) {
+    if (mbar_try_wait_sleep(bar, parity, 20000)) return true;
+    if (*abort_flag != 0u) return false;
+    if (globaltimer_ns() - t0 > p.timeout_ns) {
+      fmha_report(p, B2G_STATUS_TIMEOUT | site);
+      *abort_flag = 1u;
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ bool fmha_wait(uint32_t bar, uint32_t parity,
+                                          volatile uint32_t* abort_flag, const FmhaParams& p,
+                                          int site) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return fmha_wait_slow(bar, parity, abort_flag, p, site);
+}
+
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <bool kBF16>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  if constexpr (kBF16) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  } else {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+}
+
+template <int D, bool kBF16>
+__global__ void __launch_bounds__(192, 1) fmha_fwd_kernel(const __grid_constant__ FmhaParams p) {
+  using FP = FmhaPlan<D>;
+  constexpr uint32_t KS = FP::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int32_t m0 = static_cast<int32_t>(blockIdx.x) * 128;
+  const int32_t h = static_cast<int32_t>(blockIdx.y);
+  const int32_t b = static_cast<int32_t>(blockIdx.z);
+  const int32_t hk = h / (p.HQ / p.HK);
+  const int32_t n_kv = (p.S_k + 127) / 128;
+
+  const uint32_t bar0 = sbase + FP::kBarOff;
+  const uint32_t q_full = bar0;
+  auto k_full = [&](uint32_t s) { return bar0 + 8u * (1 + s); };
+  auto k_empty = [&](uint32_t s) { return bar0 + 8u * (1 + KS + s); };
+  auto v_full = [&](uint32_t s) { return bar0 + 8u * (1 + 2 * KS + s); };
+  auto v_empty = [&](uint32_t s) { return bar0 + 8u * (1 + 3 * KS + s); };
+  auto s_full = [&](uint32_t i) { return bar0 + 8u * (1 + 4 * KS + i); };
+  auto s_free = [&](uint32_t i) { return bar0 + 8u * (3 + 4 * KS + i); };
+  auto p_full = [&](uint32_t i) { return bar0 + 8u * (5 + 4 * KS + i); };
+  auto pv_done = [&](uint32_t i) { return bar0 + 8u * (7 + 4 * KS + i); };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + FP::kMiscOff);
+  volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + FP::kMiscOff + 4);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (uint32_t s = 0; s < KS; ++s) {
+      mbar_init(k_full(s), 1);
+      mbar_init(k_empty(s), 1);
+      mbar_init(v_full(s), 1);
+      mbar_init(v_empty(s), 1);
+    }
+    for (uint32_t i = 0; i < 2; ++i) {
+      mbar_init(s_full(i), 1);
+      mbar_init(s_free(i), 4);  // one arrival per softmax warp
+      mbar_init(p_full(i), 4);
+      mbar_init(pv_done(i), 1);
+    }
+    *abort_flag = 0u;
+    fence_mbarrier_init();
+    prefetch_tensormap(&p.tmQ);
+    prefetch_tensormap(&p.tmK);
+    prefetch_tensormap(&p.tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc<1>(smem_u32(tmem_slot), 512);
+    tmem_relinquish<1>();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer --
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, FP::kTile);
+      for (uint32_t r = 0; r < FP::kRegions; ++r)
+        tma_load_4d(sbase + FP::kQOff + r * FP::kRegion, &p.tmQ, q_full, r * 64, m0, h, b);
+      int32_t j = 0;
+      for (; j < n_kv; ++j) {
+        const uint32_t s = static_cast<uint32_t>(j) % KS, ph = (static_cast<uint32_t>(j) / KS) & 1u;
+        if (!fmha_wait(k_empty(s), ph ^ 1u, abort_flag, p, B2G_SITE_EMPTY)) break;
+        mbar_arrive_expect_tx(k_full(s), FP::kTile);
+        for (uint32_t r = 0; r < FP::kRegions; ++r)
+          tma_load_4d(sbase + FP::kKOff + s * FP::kTile + r * FP::kRegion, &p.tmK, k_full(s),
+                      r * 64, j * 128, hk, b);
+        if (!fmha_wait(v_empty(s), ph ^ 1u, abort_flag, p, B2G_SITE_EMPTY)) break;
+        mbar_arrive_expect_tx(v_full(s), FP::kTile);
+        for (uint32_t r = 0; r < FP::kRegions; ++r)
+          tma_load_4d(sbase + FP::kVOff + s * FP::kTile + r * FP::kRegion, &p.tmV, v_full(s),
+                      r * 64, j * 128, hk, b);
+      }
+      // every load issued lands before the CTA can exit
+      uint32_t spins = 0;
+      while (!mbar_try_wait(q_full, 0) && spins < (1u << 20)) ++spins;
+      for (int32_t i = j > static_cast<int32_t>(KS) ? j - static_cast<int32_t>(KS) : 0; i < j; ++i) {
+        const uint32_t s = static_cast<uint32_t>(i) % KS, ph = (static_cast<uint32_t>(i) / KS) & 1u;
+        spins = 0;
+        while (!mbar_try_wait(k_full(s), ph) && spins < (1u << 20)) ++spins;
+        spins = 0;
+        while (!mbar_try_wait(v_full(s), ph) && spins < (1u << 20)) ++spins;
+      }
+    }
+  } else if (warp == 1) {
+    // ----------------------------------------------------------- MMA issue --
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = fmha_idesc_s<D, kBF16>();
+      constexpr uint32_t idesc_pv = fmha_idesc_pv<D, kBF16>();
+      uint32_t last_bar = 0, last_par = 0;  // the newest commit: all earlier MMAs precede it
+      bool alive = fmha_wait(q_full, 0, abort_flag, p, B2G_SITE_FULL);
+      for (int32_t j = 0; alive && j <= n_kv; ++j) {
+        if (j < n_kv) {
+          // S_j = Q K_j^T into score buffer j % 2
+          const uint32_t s = static_cast<uint32_t>(j) % KS, ph = (static_cast<uint32_t>(j) / KS) & 1u;
+          const uint32_t sb = static_cast<uint32_t>(j) & 1u;
+          if (!fmha_wait(k_full(s), ph, abort_flag, p, B2G_SITE_FULL)) break;
+          if (j >= 2 && !fmha_wait(s_free(sb), ((static_cast<uint32_t>(j) - 2) >> 1) & 1u,
+                                   abort_flag, p, B2G_SITE_ACC_EMPTY))
+            break;
+          tc_fence_after();
+          const uint32_t k_base = sbase + FP::kKOff + s * FP::kTile;
+#pragma unroll
+          for (uint32_t kk = 0; kk < D / 16; ++kk) {
+            // 16 head-dim elements per MMA: slab kk / 4, +32 bytes inside the swizzled row
+            const uint64_t ad = sdesc_kmajor_sw128(sbase + FP::kQOff + (kk >> 2) * FP::kRegion) +
+                                2u * (kk & 3u);
+            const uint64_t bd = sdesc_kmajor_sw128(k_base + (kk >> 2) * FP::kRegion) + 2u * (kk & 3u);
+            mma_f16<1>(tmem_base + (sb ? FP::kS1 : FP::kS0), ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+          }
+          tc_commit<1>(s_full(sb));
+          tc_commit<1>(k_empty(s));
+          last_bar = s_full(sb);
+          last_par = (static_cast<uint32_t>(j) >> 1) & 1u;
+        }
+        if (j >= 1) {
+          // O += P_{j-1} V_{j-1}
+          const int32_t i = j - 1;
+          const uint32_t s = static_cast<uint32_t>(i) % KS, ph = (static_cast<uint32_t>(i) / KS) & 1u;
+          const uint32_t pb = static_cast<uint32_t>(i) & 1u;
+          if (!fmha_wait(p_full(pb), (static_cast<uint32_t>(i) >> 1) & 1u, abort_flag, p,
+                         B2G_SITE_ACC_FULL))
+            break;
+          if (!fmha_wait(v_full(s), ph, abort_flag, p, B2G_SITE_FULL)) break;
+          tc_fence_after();
+          const uint32_t v_base = sbase + FP::kVOff + s * FP::kTile;
+#pragma unroll
+          for (uint32_t kk = 0; kk < 128 / 16; ++kk) {
+            // 16 keys per MMA: two 8-row swizzle atoms; head-dim slabs are kRegion apart
+            const uint64_t bd = sdesc_mnmajor_sw128(v_base + kk * 2048u, FP::kRegion, 1024u);
+            mma_f16_ts(tmem_base + FP::kO, tmem_base + (pb ? FP::kP1 : FP::kP0) + kk * 8u, bd,
+                       idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit<1>(pv_done(pb));
+          tc_commit<1>(v_empty(s));
+          last_bar = pv_done(pb);
+          last_par = (static_cast<uint32_t>(i) >> 1) & 1u;
+        }
+      }
+      // all MMAs issued by this thread finish before TMEM can be freed
+      if (last_bar != 0u) {
+        uint32_t spins = 0;
+        while (!mbar_try_wait(last_bar, last_par) && spins < (1u << 22)) ++spins;
+      }
+    }
+  } else {
+    // --------------------------------------------- softmax and epilogue --
+    // Thread t of warp w owns query row 32 * (w % 4) + t: the TMEM lane
+    // quarter a warp may touch is fixed by its index in the warpgroup.
+    const uint32_t quarter = warp & 3u;
+    const uint32_t row = quarter * 32u + lane;
+    const uint32_t taddr = tmem_base + ((quarter * 32u) << 16);
+    const float sl2 = p.scale_log2;
+    float m_run = -INFINITY;  // running max of s * sl2 (log2 units) used as the exponent offset
+    float l_run = 0.0f;       // running sum of exp2(s * sl2 - m_run)
+    bool alive = true;
+    for (int32_t j = 0; j < n_kv; ++j) {
+      const uint32_t sb = static_cast<uint32_t>(j) & 1u;
+      if (!__all_sync(0xffffffffu, fmha_wait(s_full(sb), (static_cast<uint32_t>(j) >> 1) & 1u,
+                                             abort_flag, p, B2G_SITE_ACC_FULL))) {
+        alive = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t s[128];
+      {
+        uint32_t (&s0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[0]);
+        uint32_t (&s1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[32]);
+        uint32_t (&s2)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[64]);
+        uint32_t (&s3)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[96]);
+        const uint32_t sc = taddr + (sb ? FP::kS1 : FP::kS0);
+        tmem_ld_32x32b_x32(sc, s0);
+        tmem_ld_32x32b_x32(sc + 32u, s1);
+        tmem_ld_32x32b_x32(sc + 64u, s2);
+        tmem_ld_32x32b_x32(sc + 96u, s3);
+        tmem_wait_ld();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s_free(sb));  // the MMA may write S_{j+2} here now
+
+      // keys past S_k (zero-filled by TMA) take no part
+      const int32_t valid = p.S_k - j * 128;
+      if (valid < 128) {
+#pragma unroll
+        for (int c = 0; c < 128; ++c)
+          if (c >= valid) s[c] = __float_as_uint(-INFINITY);
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) mx = fmaxf(mx, __uint_as_float(s[c]));
+      // The exponent offset moves only when the row max grows by more than
+      // 2^kRescaleLog2 over it: P stays below 2^kRescaleLog2, the final 1/l
+      // cancels the offset exactly, and most tiles skip the O rescale.
+      constexpr float kRescaleLog2 = 8.0f;
+      const float m_cand = mx * sl2;
+      const bool move = m_cand > m_run + kRescaleLog2;
+      const float m_new = move ? m_cand : m_run;
+      const float alpha = move ? fast_exp2(m_run - m_new) : 1.0f;
+
+      // P_j may overwrite buffer sb once PV_{j-2} has read it
+      if (j >= 2 &&
+          !__all_sync(0xffffffffu, fmha_wait(pv_done(sb), ((static_cast<uint32_t>(j) - 2) >> 1) & 1u,
+                                             abort_flag, p, B2G_SITE_ACC_EMPTY))) {
+        alive = false;
+        break;
+      }
+      float sum = 0.0f;
+      const uint32_t pc = taddr + (sb ? FP::kP1 : FP::kP0);
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t pk[32];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const float e0 = fast_exp2(fmaf(__uint_as_float(s[half * 64 + 2 * c]), sl2, -m_new));
+          const float e1 = fast_exp2(fmaf(__uint_as_float(s[half * 64 + 2 * c + 1]), sl2, -m_new));
+          sum += e0 + e1;
+          pk[c] = pack2<kBF16>(e0, e1);
+        }
+        tmem_st_32x32b_x32(pc + static_cast<uint32_t>(half) * 32u, pk);
+      }
+      l_run = fmaf(l_run, alpha, sum);
+      m_run = m_new;
+
+      // O holds PV_0..PV_{j-1}; rows whose offset moved are scaled by alpha
+      // before PV_j adds onto them
+      if (j >= 1 && __any_sync(0xffffffffu, move)) {
+        if (!__all_sync(0xffffffffu, fmha_wait(pv_done((static_cast<uint32_t>(j) - 1) & 1u),
+                                               ((static_cast<uint32_t>(j) - 1) >> 1) & 1u,
+                                               abort_flag, p, B2G_SITE_ACC_EMPTY))) {
+          alive = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (uint32_t c0 = 0; c0 < static_cast<uint32_t>(D); c0 += 32u) {
+          uint32_t o[32];
+          tmem_ld_32x32b_x32(taddr + FP::kO + c0, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+          tmem_st_32x32b_x32(taddr + FP::kO + c0, o);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full(sb));
+    }
+
+    if (alive && n_kv > 0) {
+      const uint32_t last = static_cast<uint32_t>(n_kv - 1);
+      if (__all_sync(0xffffffffu,
+                     fmha_wait(pv_done(last & 1u), (last >> 1) & 1u, abort_flag, p, B2G_SITE_ACC_FULL))) {
+        tc_fence_after();
+        const int32_t q_row = m0 + static_cast<int32_t>(row);
+        const bool in_range = q_row < p.S_q;
+        const float inv_l = 1.0f / l_run;
+        using OutT = typename std::conditional<kBF16, __nv_bfloat16, __half>::type;
+        OutT* orow = static_cast<OutT*>(p.O) + static_cast<int64_t>(b) * p.o_sb +
+                     static_cast<int64_t>(h) * p.o_sh + static_cast<int64_t>(q_row) * p.o_ss;
+#pragma unroll
+        for (uint32_t c0 = 0; c0 < static_cast<uint32_t>(D); c0 += 32u) {
+          uint32_t o[32];
+          tmem_ld_32x32b_x32(taddr + FP::kO + c0, o);
+          tmem_wait_ld();
+          if (in_range) {
+            uint4* dst = reinterpret_cast<uint4*>(orow + c0);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint4 w;
+              w.x = pack2<kBF16>(__uint_as_float(o[8 * v + 0]) * inv_l, __uint_as_float(o[8 * v + 1]) * inv_l);
+              w.y = pack2<kBF16>(__uint_as_float(o[8 * v + 2]) * inv_l, __uint_as_float(o[8 * v + 3]) * inv_l);
+              w.z = pack2<kBF16>(__uint_as_float(o[8 * v + 4]) * inv_l, __uint_as_float(o[8 * v + 5]) * inv_l);
+              w.w = pack2<kBF16>(__uint_as_float(o[8 * v + 6]) * inv_l, __uint_as_float(o[8 * v + 7]) * inv_l);
+              dst[v] = w;
+            }
+          }
+        }
+        if (in_range && p.lse != nullptr) {
+          // natural-log log-sum-exp of the scaled scores of this row
+          constexpr float kLn2 = 0.693147180559945309f;
+          p.lse[(static_cast<int64_t>(b) * p.HQ + h) * p.S_q + q_row] = (m_run + __log2f(l_run)) * kLn2;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc<1>(tmem_base, 512);
+  }
+}
+
+// ------------------------------------------------------------------ host --
+namespace {
+
+// 4-D view (d, sequence, head, batch) of one operand, 64 x 128 boxes.
+bool encode_bshd_view(CUtensorMap* map, const void* base, int dtype, int D, int S, int H, int B,
+                      const int64_t* st /* batch, head, seq, dim (elements) */) {
+  auto enc = tma_encoder();
+  if (enc == nullptr) return false;
+  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(S),
+                              static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(B)};
+  const cuuint64_t strides[3] = {static_cast<cuuint64_t>(st[2]) * 2u,
+                                 static_cast<cuuint64_t>(st[1]) * 2u,
+                                 static_cast<cuuint64_t>(st[0]) * 2u};
+  const cuuint32_t box[4] = {64, 128, 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUtensorMapDataType t =
+      dtype == B2G_DT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return enc(map, t, 4, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int D, bool kBF16>
+int launch_fmha(const FmhaParams& prm, int batch, int heads_q, int seqlen_q, cudaStream_t stream) {
+  using FP = FmhaPlan<D>;
+  auto kern = fmha_fwd_kernel<D, kBF16>;
+  // At least half the SM's shared memory, so that two CTAs never share an SM
+  // (each holds all 512 TMEM columns).
+  const uint32_t dyn = FP::kDynBytes > 120u * 1024u ? FP::kDynBytes : 120u * 1024u;
+  static std::atomic<bool> attr_set[64];  // per instantiation and device
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return B2G_ENODEVICE;
+  }
+  if (!attr_set[dev].load()) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(dyn)) != cudaSuccess)
+      return static_cast<int>(cudaGetLastError());
+    attr_set[dev].store(true);
+  }
+  const dim3 grid(static_cast<unsigned>((seqlen_q + 127) / 128), static_cast<unsigned>(heads_q),
+                  static_cast<unsigned>(batch));
+  kern<<<grid, FP::kThreads, dyn, stream>>>(prm);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? B2G_OK : static_cast<int>(e);
+}
+
+}  // namespace
+
+}  // namespace b2g
+
+extern "C" int b2g_attention_fwd(const void* q, const void* k, const void* v, void* o,
+                                 const int64_t* strides, int batch, int heads_q, int heads_k,
+                                 int seqlen_q, int seqlen_k, int head_dim, int dtype,
+                                 float sm_scale, float* lse, int* status, void* stream) {
+  using namespace b2g;
+  if (q == nullptr || k == nullptr || v == nullptr || o == nullptr || strides == nullptr)
+    return B2G_EINVAL;
+  if (dtype != B2G_DT_F16 && dtype != B2G_DT_BF16) return B2G_EINVAL;
+  if (!(sm_scale > 0.0f) || !std::isfinite(sm_scale)) return B2G_EINVAL;
+  if (head_dim != 64 && head_dim != 128) return B2G_ESHAPE;
+  if (batch < 1 || heads_q < 1 || heads_k < 1 || heads_q % heads_k != 0) return B2G_ESHAPE;
+  if (batch > 65535 || heads_q > 65535 || seqlen_q < 0 || seqlen_k < 1) return B2G_ESHAPE;
+  for (int t = 0; t < 4; ++t) {
+    const int64_t* st = strides + 4 * t;
+    if (st[3] != 1) return B2G_ESTRIDE;
+    for (int i = 0; i < 3; ++i)
+      if (st[i] <= 0) return B2G_ESTRIDE;
+    // rows must not overlap within a head: the sequence stride covers the row
+    if (st[2] < head_dim) return B2G_ESTRIDE;
+    for (int i = 0; i < 3; ++i)
+      if ((st[i] * 2) % 16 != 0) return B2G_EALIGN;
+  }
+  for (const void* ptr : {q, k, v, static_cast<const void*>(o)})
+    if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0) return B2G_EALIGN;
+  if (current_device_sms() <= 0) return B2G_ENODEVICE;
+  if (seqlen_q == 0) return B2G_OK;
+
+  FmhaParams prm;
+  std::memset(&prm, 0, sizeof(prm));
+  if (!encode_bshd_view(&prm.tmQ, q, dtype, head_dim, seqlen_q, heads_q, batch, strides) ||
+      !encode_bshd_view(&prm.tmK, k, dtype, head_dim, seqlen_k, heads_k, batch, strides + 4) ||
+      !encode_bshd_view(&prm.tmV, v, dtype, head_dim, seqlen_k, heads_k, batch, strides + 8))
+    return B2G_ETENSORMAP;
+  prm.O = o;
+  prm.o_sb = strides[12];
+  prm.o_sh = strides[13];
+  prm.o_ss = strides[14];
+  prm.lse = lse;
+  prm.status = status;
+  prm.HQ = heads_q;
+  prm.HK = heads_k;
+  prm.S_q = seqlen_q;
+  prm.S_k = seqlen_k;
+  prm.scale_log2 = sm_scale * 1.4426950408889634f;
+  prm.timeout_ns = wait_timeout_ns();
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool bf16 = dtype == B2G_DT_BF16;
+  if (head_dim == 128)
+    return bf16 ? launch_fmha<128, true>(prm, batch, heads_q, seqlen_q, s)
+                : launch_fmha<128, false>(prm, batch, heads_q, seqlen_q, s);
+  return bf16 ? launch_fmha<64, true>(prm, batch, heads_q, seqlen_q, s)
+              : launch_fmha<64, false>(prm, batch, heads_q, seqlen_q, s);
+}

@@ -556,6 +556,13 @@ int gemm_mxf4_fixed_scratch(const uint8_t* A, int64_t lda, const uint8_t* B, int
   return run_gemm(c);
 }
 
+
+int current_device_sms() { return current_sms(); }
+
+PFN_cuTensorMapEncodeTiled_v12000 tma_encoder() { return tensor_map_encoder(); }
+
+uint64_t wait_timeout_ns() { return static_cast<uint64_t>(g_opt.timeout_ms.load()) * 1000000ull; }
+
 }  // namespace b2g
 
 extern "C" {

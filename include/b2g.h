@@ -178,6 +178,26 @@ B2G_API int b2g_gemm_mxf4_grouped(const uint8_t* A, int64_t lda, const uint8_t* 
                                   size_t workspace_bytes, int* status, void* stream);
 B2G_API size_t b2g_gemm_grouped_workspace_bytes(int M, int N, int K, int groups);
 
+/* Attention forward, non-causal, with grouped-query heads:
+ *   O[b, h] = softmax(Q[b, h] K[b, g]^T * sm_scale) V[b, g],  g = h / (heads_q / heads_k)
+ * Replaces run_gluon_attention (kernels/attention/fmha_v4.py:761-790) and the
+ * gluon_attn_fwd launch it makes; reference numerics kernels/attention/common.py:115
+ * (sdpa_reference). `strides` holds 16 element strides, four per tensor in the
+ * order q, k, v, o and, inside each, (batch, head, sequence, dim) -- the order of
+ * get_strides_from_layout (common.py:79), so bhsd and bshd layouts are both plain
+ * strides. The dim stride must be 1 and the other strides positive multiples of
+ * 8 elements; q, k, v and o 16-byte aligned. head_dim 64 or 128; dtype B2G_DT_F16
+ * or B2G_DT_BF16 for all four tensors; heads_q a multiple of heads_k; seqlen_k >= 1
+ * and any seqlen_q >= 0 (unlike the reference, neither needs to be a multiple of
+ * a block size, nor equal). `lse`, when not null, receives the natural-log
+ * log-sum-exp of each row's scaled scores as float [batch][heads_q][seqlen_q]
+ * (the reference keeps this in its internal M buffer). Accumulation is fp32;
+ * P is rounded to the input type before the PV product. */
+B2G_API int b2g_attention_fwd(const void* q, const void* k, const void* v, void* o,
+                              const int64_t* strides, int batch, int heads_q, int heads_k,
+                              int seqlen_q, int seqlen_k, int head_dim, int dtype,
+                              float sm_scale, float* lse, int* status, void* stream);
+
 /* Blocked E8M0 scale layout: for each 128-row block and each group of 4
  * k-blocks (4 scales), 512 bytes in which byte r0*16 + r1*4 + j holds the
  * scale of row 128*block + 32*r1 + r0 for k-block 4*group + j; blocks are
