@@ -3,20 +3,23 @@
 // (kernels/attention/fmha_v4.py:343-758, launcher :761-790; torch oracle
 // kernels/attention/common.py:115-138 sdpa_reference).
 //
-// One CTA per (128 query rows, query head, batch). Per KV tile of 128 keys:
-//   S_j  = Q K_j^T           tcgen05.mma into one of two TMEM score buffers
-//   P_j  = exp2(S_j*s' - m)  softmax warps, one query row per thread, P stored
-//                            back to TMEM as 16-bit values
-//   O   += P_j V_j           tcgen05.mma with A = P read from TMEM and B = V as an
-//                            MN-major shared-memory operand (no transpose pass)
-// The MMA thread issues S_{j+1} before PV_j, so the next score tile is computed
-// while the softmax of this one runs. The running max m is kept in log2 units
-// (s' = sm_scale * log2 e); when a row's max moves, its O row is rescaled in
-// TMEM by exp2(m_old - m_new) before PV_j accumulates.
+// One CTA per (256 query rows = two 128-row tiles, query head, batch). Per
+// tile t and KV tile j of 128 keys:
+//   S_t  = Q_t K_j^T          tcgen05.mma into tile t's TMEM score buffer
+//   P_t  = exp2(S_t*s' - m)   softmax warpgroup t, one query row per thread; P is
+//                             stored back to TMEM as 16-bit values over the
+//                             upper half of S_t's columns
+//   O_t += P_t V_j            tcgen05.mma with A = P read from TMEM and B = V as an
+//                             MN-major shared-memory operand (no transpose pass)
+// The MMA thread interleaves the tiles (PV_0, S_0 next, PV_1, S_1 next, ...) so
+// one tile's softmax runs while the tensor pipe works on the other tile. The
+// exponent offset m is kept in log2 units (s' = sm_scale * log2 e) and moves
+// only when a row max grows by more than 2^8; O rows are then rescaled in TMEM
+// before the next PV accumulates.
 //
-// CTA layout (192 threads): warp 0 one-thread TMA producer (Q once; K and V
+// CTA layout (320 threads): warp 0 one-thread TMA producer (Q once; K and V
 // through two-stage rings), warp 1 one-thread MMA issuer (owns the 512 TMEM
-// columns), warps 2-5 softmax and epilogue (TMEM lane quarter w % 4). Q, K,
+// columns), warps 2-5 and 6-9 the softmax and epilogue of tiles 0 and 1. Q, K,
 // V and O are addressed through 4-D views (d, sequence, head, batch) built
 // from the caller's strides, so bhsd and bshd layouts and GQA (query head h
 // reads key/value head h / (HQ / HK)) need no copies; keys and query rows
@@ -38,6 +41,12 @@
 #include "capi_internal.h"
 #include "ptx.cuh"
 
+// Exponential pairs per four computed by poly_exp2 on the FMA pipe instead of
+// the MUFU unit (0..4).
+#ifndef B2G_FMHA_POLY_PAIRS
+#define B2G_FMHA_POLY_PAIRS 0
+#endif
+
 namespace b2g {
 
 struct alignas(64) FmhaParams {
@@ -51,28 +60,59 @@ struct alignas(64) FmhaParams {
   uint64_t timeout_ns;
 };
 
+// Shared memory and TMEM plan of one CTA: two 128-row query tiles (Q0, Q1),
+// K and V rings, and per tile one score buffer (P aliases its upper half once
+// the scores are in registers) and one O accumulator.
 template <int D>
 struct FmhaPlan {
-  static constexpr uint32_t kThreads = 192;
+  static constexpr uint32_t kSoftmaxWarps = 8;                  // two warpgroups, one per tile
+  static constexpr uint32_t kThreads = 64 + 32 * kSoftmaxWarps;  // + producer and MMA warps
   static constexpr uint32_t kRegions = D / 64;             // 64-element (128-byte) column slabs
   static constexpr uint32_t kRegion = 128 * 128;           // 128 rows x 128 bytes
-  static constexpr uint32_t kTile = kRegions * kRegion;    // Q, one K or one V tile
+  static constexpr uint32_t kTile = kRegions * kRegion;    // one Q, K or V tile
   static constexpr uint32_t kStages = 2;                   // K ring and V ring depth
-  static constexpr uint32_t kQOff = 0;
-  static constexpr uint32_t kKOff = kQOff + kTile;
+  static constexpr uint32_t kQOff = 0;                     // Q0, Q1
+  static constexpr uint32_t kKOff = kQOff + 2 * kTile;
   static constexpr uint32_t kVOff = kKOff + kStages * kTile;
   static constexpr uint32_t kBarOff = kVOff + kStages * kTile;
-  // q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], s_free[2],
-  // p_full[2], pv_done[2]
-  static constexpr uint32_t kNumBars = 1 + 4 * kStages + 8;
+  // q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_full[2], o_done[2]
+  static constexpr uint32_t kNumBars = 1 + 4 * kStages + 6;
   static constexpr uint32_t kMiscOff = kBarOff + kNumBars * 8;  // tmem slot, abort flag
   static constexpr uint32_t kBytes = kMiscOff + 16;
   static constexpr uint32_t kDynBytes = kBytes + 1024;  // + alignment slack
-  // TMEM columns: S0, S1 (128 fp32 each), O (D fp32), P0, P1 (64 x 2 x 16-bit each)
-  static constexpr uint32_t kS0 = 0, kS1 = 128, kO = 256, kP0 = 384, kP1 = 448;
+  // TMEM columns: S_t = 128 t (128 fp32), P_t = S_t + 64 (128 x 16-bit),
+  // O_t = 256 + 128 t (D fp32)
+  static constexpr uint32_t kS = 0, kP = 64, kO = 256, kTileCols = 128;
   static_assert(D == 64 || D == 128, "head dim");
   static_assert(kDynBytes <= 232448, "shared memory");
 };
+
+// exp2 on the FMA pipe for x <= 8 (a share of the softmax exponentials, so that
+// they do not all queue on the MUFU unit): x = i + f with i = round(x) and
+// f in [-0.5, 0.5]; 2^f from a cubic fitted here to minimise the relative error
+// on that interval (iteratively reweighted least squares; max relative error
+// 7.5e-5 in fp32, below half an fp16 ULP); 2^i added to the exponent field.
+// Inputs below -126 (masked keys are -inf) are clamped there: with 2^f in
+// [0.70, 1.42] the biased exponent 126 or 127 plus i >= -126 stays >= 0, so the
+// result is a tiny non-negative number, never a carry into the sign bit.
+__device__ __forceinline__ float poly_exp2(float x) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23: adding it rounds to an integer
+  x = fmaxf(x, -126.0f);
+  const float t = x + kRound;
+  const float fi = t - kRound;
+  const float f = x - fi;
+  float p = fmaf(0.05517134442925453f, f, 0.24261033535003662f);
+  p = fmaf(p, f, 0.6932609677314758f);
+  p = fmaf(p, f, 0.9999281167984009f);
+  const int32_t i = static_cast<int32_t>(__float_as_uint(t) - __float_as_uint(kRound));
+  return __uint_as_float(static_cast<uint32_t>(static_cast<int32_t>(__float_as_uint(p)) + (i << 23)));
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float m;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(m) : "f"(a), "f"(b), "f"(c));
+  return m;
+}
 
 template <int D, bool kBF16>
 __host__ __device__ constexpr uint32_t fmha_idesc_s() {
@@ -137,7 +177,8 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 }
 
 template <int D, bool kBF16>
-__global__ void __launch_bounds__(192, 1) fmha_fwd_kernel(const __grid_constant__ FmhaParams p) {
+__global__ void __launch_bounds__(FmhaPlan<D>::kThreads, 1)
+    fmha_fwd_kernel(const __grid_constant__ FmhaParams p) {
   using FP = FmhaPlan<D>;
   constexpr uint32_t KS = FP::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -145,11 +186,12 @@ __global__ void __launch_bounds__(192, 1) fmha_fwd_kernel(const __grid_constant_
                                              ~static_cast<uintptr_t>(1023));
   const uint32_t sbase = smem_u32(smem);
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int32_t m0 = static_cast<int32_t>(blockIdx.x) * 128;
+  const int32_t m0 = static_cast<int32_t>(blockIdx.x) * 256;
   const int32_t h = static_cast<int32_t>(blockIdx.y);
   const int32_t b = static_cast<int32_t>(blockIdx.z);
   const int32_t hk = h / (p.HQ / p.HK);
   const int32_t n_kv = (p.S_k + 127) / 128;
+  const uint32_t n_tiles = p.S_q - m0 > 128 ? 2u : 1u;  // query tiles holding rows
 
   const uint32_t bar0 = sbase + FP::kBarOff;
   const uint32_t q_full = bar0;
@@ -157,10 +199,9 @@ __global__ void __launch_bounds__(192, 1) fmha_fwd_kernel(const __grid_constant_
   auto k_empty = [&](uint32_t s) { return bar0 + 8u * (1 + KS + s); };
   auto v_full = [&](uint32_t s) { return bar0 + 8u * (1 + 2 * KS + s); };
   auto v_empty = [&](uint32_t s) { return bar0 + 8u * (1 + 3 * KS + s); };
-  auto s_full = [&](uint32_t i) { return bar0 + 8u * (1 + 4 * KS + i); };
-  auto s_free = [&](uint32_t i) { return bar0 + 8u * (3 + 4 * KS + i); };
-  auto p_full = [&](uint32_t i) { return bar0 + 8u * (5 + 4 * KS + i); };
-  auto pv_done = [&](uint32_t i) { return bar0 + 8u * (7 + 4 * KS + i); };
+  auto s_full = [&](uint32_t t) { return bar0 + 8u * (1 + 4 * KS + t); };
+  auto p_full = [&](uint32_t t) { return bar0 + 8u * (3 + 4 * KS + t); };
+  auto o_done = [&](uint32_t t) { return bar0 + 8u * (5 + 4 * KS + t); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + FP::kMiscOff);
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + FP::kMiscOff + 4);
 
@@ -172,11 +213,10 @@ __global__ void __launch_bounds__(192, 1) fmha_fwd_kernel(const __grid_constant_
       mbar_init(v_full(s), 1);
       mbar_init(v_empty(s), 1);
     }
-    for (uint32_t i = 0; i < 2; ++i) {
-      mbar_init(s_full(i), 1);
-      mbar_init(s_free(i), 4);  // one arrival per softmax warp
-      mbar_init(p_full(i), 4);
-      mbar_init(pv_done(i), 1);
+    for (uint32_t t = 0; t < 2; ++t) {
+      mbar_init(s_full(t), 1);
+      mbar_init(p_full(t), 4);  // one arrival per softmax warp of the tile
+      mbar_init(o_done(t), 1);
     }
     *abort_flag = 0u;
     fence_mbarrier_init();
@@ -196,9 +236,11 @@ __global__ void __launch_bounds__(192, 1) fmha_fwd_kernel(const __grid_constant_
   if (warp == 0) {
     // ------------------------------------------------------------ producer --
     if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, FP::kTile);
-      for (uint32_t r = 0; r < FP::kRegions; ++r)
-        tma_load_4d(sbase + FP::kQOff + r * FP::kRegion, &p.tmQ, q_full, r * 64, m0, h, b);
+      mbar_arrive_expect_tx(q_full, n_tiles * FP::kTile);
+      for (uint32_t t = 0; t < n_tiles; ++t)
+        for (uint32_t r = 0; r < FP::kRegions; ++r)
+          tma_load_4d(sbase + FP::kQOff + t * FP::kTile + r * FP::kRegion, &p.tmQ, q_full,
+                      r * 64, m0 + static_cast<int32_t>(t) * 128, h, b);
       int32_t j = 0;
       for (; j < n_kv; ++j) {
         const uint32_t s = static_cast<uint32_t>(j) % KS, ph = (static_cast<uint32_t>(j) / KS) & 1u;
@@ -226,58 +268,78 @@ __global__ void __launch_bounds__(192, 1) fmha_fwd_kernel(const __grid_constant_
     }
   } else if (warp == 1) {
     // ----------------------------------------------------------- MMA issue --
+    // Per tile the order is S_0, PV_0, S_1, PV_1, ...: P_j lives in S's
+    // columns, and the tensor pipe runs one thread's MMAs in issue order, so
+    // S_{j+1} is issued only after PV_j. The two tiles interleave: while one
+    // tile's softmax runs, the other tile's PV and next S keep the pipe busy.
     if (lane == 0) {
       constexpr uint32_t idesc_s = fmha_idesc_s<D, kBF16>();
       constexpr uint32_t idesc_pv = fmha_idesc_pv<D, kBF16>();
       uint32_t last_bar = 0, last_par = 0;  // the newest commit: all earlier MMAs precede it
-      bool alive = fmha_wait(q_full, 0, abort_flag, p, B2G_SITE_FULL);
-      for (int32_t j = 0; alive && j <= n_kv; ++j) {
-        if (j < n_kv) {
-          // S_j = Q K_j^T into score buffer j % 2
-          const uint32_t s = static_cast<uint32_t>(j) % KS, ph = (static_cast<uint32_t>(j) / KS) & 1u;
-          const uint32_t sb = static_cast<uint32_t>(j) & 1u;
-          if (!fmha_wait(k_full(s), ph, abort_flag, p, B2G_SITE_FULL)) break;
-          if (j >= 2 && !fmha_wait(s_free(sb), ((static_cast<uint32_t>(j) - 2) >> 1) & 1u,
-                                   abort_flag, p, B2G_SITE_ACC_EMPTY))
-            break;
-          tc_fence_after();
-          const uint32_t k_base = sbase + FP::kKOff + s * FP::kTile;
+      auto issue_s = [&](uint32_t t, uint32_t kslot) {
+        const uint32_t k_base = sbase + FP::kKOff + kslot * FP::kTile;
+        const uint32_t q_base = sbase + FP::kQOff + t * FP::kTile;
 #pragma unroll
-          for (uint32_t kk = 0; kk < D / 16; ++kk) {
-            // 16 head-dim elements per MMA: slab kk / 4, +32 bytes inside the swizzled row
-            const uint64_t ad = sdesc_kmajor_sw128(sbase + FP::kQOff + (kk >> 2) * FP::kRegion) +
-                                2u * (kk & 3u);
-            const uint64_t bd = sdesc_kmajor_sw128(k_base + (kk >> 2) * FP::kRegion) + 2u * (kk & 3u);
-            mma_f16<1>(tmem_base + (sb ? FP::kS1 : FP::kS0), ad, bd, idesc_s, kk > 0 ? 1u : 0u);
-          }
-          tc_commit<1>(s_full(sb));
-          tc_commit<1>(k_empty(s));
-          last_bar = s_full(sb);
-          last_par = (static_cast<uint32_t>(j) >> 1) & 1u;
+        for (uint32_t kk = 0; kk < D / 16; ++kk) {
+          // 16 head-dim elements per MMA: slab kk / 4, +32 bytes inside the swizzled row
+          const uint64_t ad = sdesc_kmajor_sw128(q_base + (kk >> 2) * FP::kRegion) + 2u * (kk & 3u);
+          const uint64_t bd = sdesc_kmajor_sw128(k_base + (kk >> 2) * FP::kRegion) + 2u * (kk & 3u);
+          mma_f16<1>(tmem_base + FP::kS + t * FP::kTileCols, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
         }
-        if (j >= 1) {
-          // O += P_{j-1} V_{j-1}
-          const int32_t i = j - 1;
-          const uint32_t s = static_cast<uint32_t>(i) % KS, ph = (static_cast<uint32_t>(i) / KS) & 1u;
-          const uint32_t pb = static_cast<uint32_t>(i) & 1u;
-          if (!fmha_wait(p_full(pb), (static_cast<uint32_t>(i) >> 1) & 1u, abort_flag, p,
-                         B2G_SITE_ACC_FULL))
+      };
+      bool alive = fmha_wait(q_full, 0, abort_flag, p, B2G_SITE_FULL) &&
+                   fmha_wait(k_full(0), 0, abort_flag, p, B2G_SITE_FULL);
+      if (alive) {
+        tc_fence_after();
+        for (uint32_t t = 0; t < n_tiles; ++t) {
+          issue_s(t, 0);
+          tc_commit<1>(s_full(t));
+        }
+        tc_commit<1>(k_empty(0));
+        last_bar = k_empty(0);
+        last_par = 0;
+      }
+      for (int32_t j = 0; alive && j < n_kv; ++j) {
+        const uint32_t s = static_cast<uint32_t>(j) % KS, ph = (static_cast<uint32_t>(j) / KS) & 1u;
+        const bool has_next = j + 1 < n_kv;
+        const uint32_t s1 = static_cast<uint32_t>(j + 1) % KS;
+        const uint32_t ph1 = (static_cast<uint32_t>(j + 1) / KS) & 1u;
+        if (!fmha_wait(v_full(s), ph, abort_flag, p, B2G_SITE_FULL)) break;
+        const uint32_t v_base = sbase + FP::kVOff + s * FP::kTile;
+        for (uint32_t t = 0; alive && t < n_tiles; ++t) {
+          if (!fmha_wait(p_full(t), static_cast<uint32_t>(j) & 1u, abort_flag, p,
+                         B2G_SITE_ACC_FULL)) {
+            alive = false;
             break;
-          if (!fmha_wait(v_full(s), ph, abort_flag, p, B2G_SITE_FULL)) break;
+          }
           tc_fence_after();
-          const uint32_t v_base = sbase + FP::kVOff + s * FP::kTile;
+          const uint32_t p_col = tmem_base + FP::kS + t * FP::kTileCols + FP::kP;
 #pragma unroll
           for (uint32_t kk = 0; kk < 128 / 16; ++kk) {
             // 16 keys per MMA: two 8-row swizzle atoms; head-dim slabs are kRegion apart
             const uint64_t bd = sdesc_mnmajor_sw128(v_base + kk * 2048u, FP::kRegion, 1024u);
-            mma_f16_ts(tmem_base + FP::kO, tmem_base + (pb ? FP::kP1 : FP::kP0) + kk * 8u, bd,
-                       idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
+            mma_f16_ts(tmem_base + FP::kO + t * FP::kTileCols, p_col + kk * 8u, bd, idesc_pv,
+                       (j > 0 || kk > 0) ? 1u : 0u);
           }
-          tc_commit<1>(pv_done(pb));
-          tc_commit<1>(v_empty(s));
-          last_bar = pv_done(pb);
-          last_par = (static_cast<uint32_t>(i) >> 1) & 1u;
+          if (!has_next) {
+            tc_commit<1>(o_done(t));
+            last_bar = o_done(t);
+            last_par = 0;
+            continue;
+          }
+          if (t == 0 && !fmha_wait(k_full(s1), ph1, abort_flag, p, B2G_SITE_FULL)) {
+            alive = false;
+            break;
+          }
+          tc_fence_after();
+          issue_s(t, s1);
+          tc_commit<1>(s_full(t));
+          last_bar = s_full(t);
+          last_par = static_cast<uint32_t>(j + 1) & 1u;
         }
+        if (!alive) break;
+        tc_commit<1>(v_empty(s));
+        if (has_next) tc_commit<1>(k_empty(s1));
       }
       // all MMAs issued by this thread finish before TMEM can be freed
       if (last_bar != 0u) {
@@ -287,115 +349,111 @@ __global__ void __launch_bounds__(192, 1) fmha_fwd_kernel(const __grid_constant_
     }
   } else {
     // --------------------------------------------- softmax and epilogue --
-    // Thread t of warp w owns query row 32 * (w % 4) + t: the TMEM lane
-    // quarter a warp may touch is fixed by its index in the warpgroup.
-    const uint32_t quarter = warp & 3u;
-    const uint32_t row = quarter * 32u + lane;
-    const uint32_t taddr = tmem_base + ((quarter * 32u) << 16);
-    const float sl2 = p.scale_log2;
-    float m_run = -INFINITY;  // running max of s * sl2 (log2 units) used as the exponent offset
-    float l_run = 0.0f;       // running sum of exp2(s * sl2 - m_run)
-    bool alive = true;
-    for (int32_t j = 0; j < n_kv; ++j) {
-      const uint32_t sb = static_cast<uint32_t>(j) & 1u;
-      if (!__all_sync(0xffffffffu, fmha_wait(s_full(sb), (static_cast<uint32_t>(j) >> 1) & 1u,
-                                             abort_flag, p, B2G_SITE_ACC_FULL))) {
-        alive = false;
-        break;
-      }
-      tc_fence_after();
-      uint32_t s[128];
-      {
-        uint32_t (&s0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[0]);
-        uint32_t (&s1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[32]);
-        uint32_t (&s2)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[64]);
-        uint32_t (&s3)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[96]);
-        const uint32_t sc = taddr + (sb ? FP::kS1 : FP::kS0);
-        tmem_ld_32x32b_x32(sc, s0);
-        tmem_ld_32x32b_x32(sc + 32u, s1);
-        tmem_ld_32x32b_x32(sc + 64u, s2);
-        tmem_ld_32x32b_x32(sc + 96u, s3);
-        tmem_wait_ld();
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(s_free(sb));  // the MMA may write S_{j+2} here now
-
-      // keys past S_k (zero-filled by TMA) take no part
-      const int32_t valid = p.S_k - j * 128;
-      if (valid < 128) {
-#pragma unroll
-        for (int c = 0; c < 128; ++c)
-          if (c >= valid) s[c] = __float_as_uint(-INFINITY);
-      }
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 128; ++c) mx = fmaxf(mx, __uint_as_float(s[c]));
-      // The exponent offset moves only when the row max grows by more than
-      // 2^kRescaleLog2 over it: P stays below 2^kRescaleLog2, the final 1/l
-      // cancels the offset exactly, and most tiles skip the O rescale.
-      constexpr float kRescaleLog2 = 8.0f;
-      const float m_cand = mx * sl2;
-      const bool move = m_cand > m_run + kRescaleLog2;
-      const float m_new = move ? m_cand : m_run;
-      const float alpha = move ? fast_exp2(m_run - m_new) : 1.0f;
-
-      // P_j may overwrite buffer sb once PV_{j-2} has read it
-      if (j >= 2 &&
-          !__all_sync(0xffffffffu, fmha_wait(pv_done(sb), ((static_cast<uint32_t>(j) - 2) >> 1) & 1u,
-                                             abort_flag, p, B2G_SITE_ACC_EMPTY))) {
-        alive = false;
-        break;
-      }
-      float sum = 0.0f;
-      const uint32_t pc = taddr + (sb ? FP::kP1 : FP::kP0);
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t pk[32];
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float e0 = fast_exp2(fmaf(__uint_as_float(s[half * 64 + 2 * c]), sl2, -m_new));
-          const float e1 = fast_exp2(fmaf(__uint_as_float(s[half * 64 + 2 * c + 1]), sl2, -m_new));
-          sum += e0 + e1;
-          pk[c] = pack2<kBF16>(e0, e1);
-        }
-        tmem_st_32x32b_x32(pc + static_cast<uint32_t>(half) * 32u, pk);
-      }
-      l_run = fmaf(l_run, alpha, sum);
-      m_run = m_new;
-
-      // O holds PV_0..PV_{j-1}; rows whose offset moved are scaled by alpha
-      // before PV_j adds onto them
-      if (j >= 1 && __any_sync(0xffffffffu, move)) {
-        if (!__all_sync(0xffffffffu, fmha_wait(pv_done((static_cast<uint32_t>(j) - 1) & 1u),
-                                               ((static_cast<uint32_t>(j) - 1) >> 1) & 1u,
-                                               abort_flag, p, B2G_SITE_ACC_EMPTY))) {
+    // Warpgroup t (warps 2 + 4t .. 5 + 4t) owns query tile t; thread i of warp w
+    // owns row 32 * (w % 4) + i of it: the TMEM lane quarter a warp may touch
+    // is fixed by its index in the warpgroup.
+    const uint32_t t = (warp - 2u) >> 2;
+    if (t < n_tiles) {
+      const uint32_t quarter = warp & 3u;
+      const uint32_t row = quarter * 32u + lane;
+      const uint32_t taddr = tmem_base + ((quarter * 32u) << 16);
+      const uint32_t s_col = taddr + FP::kS + t * FP::kTileCols;
+      const uint32_t p_col = s_col + FP::kP;
+      const uint32_t o_col = taddr + FP::kO + t * FP::kTileCols;
+      const float sl2 = p.scale_log2;
+      float m_run = -INFINITY;  // exponent offset, log2 units (a running max of s * sl2)
+      float l_run = 0.0f;       // running sum of exp2(s * sl2 - m_run)
+      bool alive = true;
+      for (int32_t j = 0; j < n_kv; ++j) {
+        if (!__all_sync(0xffffffffu, fmha_wait(s_full(t), static_cast<uint32_t>(j) & 1u,
+                                               abort_flag, p, B2G_SITE_ACC_FULL))) {
           alive = false;
           break;
         }
         tc_fence_after();
-#pragma unroll
-        for (uint32_t c0 = 0; c0 < static_cast<uint32_t>(D); c0 += 32u) {
-          uint32_t o[32];
-          tmem_ld_32x32b_x32(taddr + FP::kO + c0, o);
+        uint32_t s[128];
+        {
+          uint32_t (&s0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[0]);
+          uint32_t (&s1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[32]);
+          uint32_t (&s2)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[64]);
+          uint32_t (&s3)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[96]);
+          tmem_ld_32x32b_x32(s_col, s0);
+          tmem_ld_32x32b_x32(s_col + 32u, s1);
+          tmem_ld_32x32b_x32(s_col + 64u, s2);
+          tmem_ld_32x32b_x32(s_col + 96u, s3);
           tmem_wait_ld();
-#pragma unroll
-          for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-          tmem_st_32x32b_x32(taddr + FP::kO + c0, o);
         }
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_full(sb));
-    }
+        // keys past S_k (zero-filled by TMA) take no part
+        const int32_t valid = p.S_k - j * 128;
+        if (valid < 128) {
+#pragma unroll
+          for (int c = 0; c < 128; ++c)
+            if (c >= valid) s[c] = __float_as_uint(-INFINITY);
+        }
+        float mx0 = __uint_as_float(s[0]), mx1 = __uint_as_float(s[1]);
+#pragma unroll
+        for (int c = 2; c < 126; c += 4) {
+          mx0 = fmax3(mx0, __uint_as_float(s[c]), __uint_as_float(s[c + 1]));
+          mx1 = fmax3(mx1, __uint_as_float(s[c + 2]), __uint_as_float(s[c + 3]));
+        }
+        const float mx = fmax3(mx0, mx1, fmaxf(__uint_as_float(s[126]), __uint_as_float(s[127])));
+        // The exponent offset moves only when the row max grows by more than
+        // 2^kRescaleLog2 over it: P stays below 2^kRescaleLog2, the final 1/l
+        // cancels the offset exactly, and most tiles skip the O rescale.
+        constexpr float kRescaleLog2 = 8.0f;
+        const float m_cand = mx * sl2;
+        const bool move = m_cand > m_run + kRescaleLog2;
+        const float m_new = move ? m_cand : m_run;
+        const float alpha = move ? fast_exp2(m_run - m_new) : 1.0f;
 
-    if (alive && n_kv > 0) {
-      const uint32_t last = static_cast<uint32_t>(n_kv - 1);
-      if (__all_sync(0xffffffffu,
-                     fmha_wait(pv_done(last & 1u), (last >> 1) & 1u, abort_flag, p, B2G_SITE_ACC_FULL))) {
+        float sum0 = 0.0f, sum1 = 0.0f;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t pk[32];
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const float x0 = fmaf(__uint_as_float(s[half * 64 + 2 * c]), sl2, -m_new);
+            const float x1 = fmaf(__uint_as_float(s[half * 64 + 2 * c + 1]), sl2, -m_new);
+            float e0, e1;
+            if ((c & 3) < B2G_FMHA_POLY_PAIRS) {  // this share on the FMA pipe
+              e0 = poly_exp2(x0);
+              e1 = poly_exp2(x1);
+            } else {
+              e0 = fast_exp2(x0);
+              e1 = fast_exp2(x1);
+            }
+            sum0 += e0;
+            sum1 += e1;
+            pk[c] = pack2<kBF16>(e0, e1);
+          }
+          tmem_st_32x32b_x32(p_col + static_cast<uint32_t>(half) * 32u, pk);
+        }
+        l_run = fmaf(l_run, alpha, sum0 + sum1);
+        m_run = m_new;
+
+        // O holds PV_0..PV_{j-1} (the S_j commit follows them); rows whose
+        // offset moved are scaled by alpha before PV_j adds onto them
+        if (j >= 1 && __any_sync(0xffffffffu, move)) {
+#pragma unroll
+          for (uint32_t c0 = 0; c0 < static_cast<uint32_t>(D); c0 += 32u) {
+            uint32_t o[32];
+            tmem_ld_32x32b_x32(o_col + c0, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+            tmem_st_32x32b_x32(o_col + c0, o);
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full(t));
+      }
+
+      if (alive && n_kv > 0 &&
+          __all_sync(0xffffffffu, fmha_wait(o_done(t), 0, abort_flag, p, B2G_SITE_ACC_FULL))) {
         tc_fence_after();
-        const int32_t q_row = m0 + static_cast<int32_t>(row);
+        const int32_t q_row = m0 + static_cast<int32_t>(t * 128u + row);
         const bool in_range = q_row < p.S_q;
         const float inv_l = 1.0f / l_run;
         using OutT = typename std::conditional<kBF16, __nv_bfloat16, __half>::type;
@@ -404,7 +462,7 @@ __global__ void __launch_bounds__(192, 1) fmha_fwd_kernel(const __grid_constant_
 #pragma unroll
         for (uint32_t c0 = 0; c0 < static_cast<uint32_t>(D); c0 += 32u) {
           uint32_t o[32];
-          tmem_ld_32x32b_x32(taddr + FP::kO + c0, o);
+          tmem_ld_32x32b_x32(o_col + c0, o);
           tmem_wait_ld();
           if (in_range) {
             uint4* dst = reinterpret_cast<uint4*>(orow + c0);
@@ -477,7 +535,7 @@ int launch_fmha(const FmhaParams& prm, int batch, int heads_q, int seqlen_q, cud
       return static_cast<int>(cudaGetLastError());
     attr_set[dev].store(true);
   }
-  const dim3 grid(static_cast<unsigned>((seqlen_q + 127) / 128), static_cast<unsigned>(heads_q),
+  const dim3 grid(static_cast<unsigned>((seqlen_q + 255) / 256), static_cast<unsigned>(heads_q),
                   static_cast<unsigned>(batch));
   kern<<<grid, FP::kThreads, dyn, stream>>>(prm);
   const cudaError_t e = cudaGetLastError();
