@@ -47,6 +47,27 @@
 #define B2G_FMHA_POLY_PAIRS 0
 #endif
 
+// 1: the two tiles' softmax exponentials take strict turns on the MUFU unit.
+#ifndef B2G_FMHA_ORDER
+#define B2G_FMHA_ORDER 0
+#endif
+
+// Exponential pairs of a tile left when its softmax hands the MUFU turn to the
+// other tile (1..32).
+#ifndef B2G_FMHA_TURN_EARLY
+#define B2G_FMHA_TURN_EARLY 4
+#endif
+
+// 1: the row max uses three-input maxima.
+#ifndef B2G_FMHA_MAX3
+#define B2G_FMHA_MAX3 1
+#endif
+
+// Suspend-time hint of the slow path of the bounded waits (0: plain probes).
+#ifndef B2G_FMHA_WAIT_HINT_NS
+#define B2G_FMHA_WAIT_HINT_NS 20000
+#endif
+
 namespace b2g {
 
 struct alignas(64) FmhaParams {
@@ -75,8 +96,9 @@ struct FmhaPlan {
   static constexpr uint32_t kKOff = kQOff + 2 * kTile;
   static constexpr uint32_t kVOff = kKOff + kStages * kTile;
   static constexpr uint32_t kBarOff = kVOff + kStages * kTile;
-  // q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_full[2], o_done[2]
-  static constexpr uint32_t kNumBars = 1 + 4 * kStages + 6;
+  // q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_full[2][2]
+  // (tile, key half), o_done[2], turn[2]
+  static constexpr uint32_t kNumBars = 1 + 4 * kStages + 10;
   static constexpr uint32_t kMiscOff = kBarOff + kNumBars * 8;  // tmem slot, abort flag
   static constexpr uint32_t kBytes = kMiscOff + 16;
   static constexpr uint32_t kDynBytes = kBytes + 1024;  // + alignment slack
@@ -106,6 +128,25 @@ __device__ __forceinline__ float poly_exp2(float x) {
   p = fmaf(p, f, 0.9999281167984009f);
   const int32_t i = static_cast<int32_t>(__float_as_uint(t) - __float_as_uint(kRound));
   return __uint_as_float(static_cast<uint32_t>(static_cast<int32_t>(__float_as_uint(p)) + (i << 23)));
+}
+
+// poly_exp2 on a pair, with the packed (two-lane) fp32 add and FMA: per pair
+// two clamps, five packed operations and two integer adds.
+__device__ __forceinline__ float2 poly_exp2x2(float2 x) {
+  constexpr float kRound = 12582912.0f;
+  x.x = fmaxf(x.x, -126.0f);
+  x.y = fmaxf(x.y, -126.0f);
+  const float2 t = __fadd2_rn(x, make_float2(kRound, kRound));
+  const float2 fi = __fadd2_rn(t, make_float2(-kRound, -kRound));
+  const float2 f = __ffma2_rn(fi, make_float2(-1.0f, -1.0f), x);
+  float2 q = __ffma2_rn(make_float2(0.05517134442925453f, 0.05517134442925453f), f,
+                        make_float2(0.24261033535003662f, 0.24261033535003662f));
+  q = __ffma2_rn(q, f, make_float2(0.6932609677314758f, 0.6932609677314758f));
+  q = __ffma2_rn(q, f, make_float2(0.9999281167984009f, 0.9999281167984009f));
+  // t's bit pattern is that of 1.5 * 2^23 plus round(x), and the former ends in
+  // nine zero bits: shifted left by 23 it leaves round(x) * 2^23, the exponent step
+  return make_float2(__uint_as_float(__float_as_uint(q.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(q.y) + (__float_as_uint(t.y) << 23)));
 }
 
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
@@ -142,7 +183,11 @@ __device__ __noinline__ bool fmha_wait_slow(uint32_t bar, uint32_t parity,
   const uint64_t t0 = globaltimer_ns();
 #pragma unroll 1
   while (true) {
-    if (mbar_try_wait_sleep(bar, parity, 20000)) return true;
+#if B2G_FMHA_WAIT_HINT_NS > 0
+    if (mbar_try_wait_sleep(bar, parity, B2G_FMHA_WAIT_HINT_NS)) return true;
+#else
+    if (mbar_try_wait(bar, parity)) return true;
+#endif
     if (*abort_flag != 0u) return false;
     if (globaltimer_ns() - t0 > p.timeout_ns) {
       fmha_report(p, B2G_STATUS_TIMEOUT | site);
@@ -200,8 +245,10 @@ __global__ void __launch_bounds__(FmhaPlan<D>::kThreads, 1)
   auto v_full = [&](uint32_t s) { return bar0 + 8u * (1 + 2 * KS + s); };
   auto v_empty = [&](uint32_t s) { return bar0 + 8u * (1 + 3 * KS + s); };
   auto s_full = [&](uint32_t t) { return bar0 + 8u * (1 + 4 * KS + t); };
-  auto p_full = [&](uint32_t t) { return bar0 + 8u * (3 + 4 * KS + t); };
-  auto o_done = [&](uint32_t t) { return bar0 + 8u * (5 + 4 * KS + t); };
+  auto p_full = [&](uint32_t t, uint32_t half) { return bar0 + 8u * (3 + 4 * KS + 2 * t + half); };
+  auto o_done = [&](uint32_t t) { return bar0 + 8u * (7 + 4 * KS + t); };
+  // turn(t): tile t's softmax may start its exponentials (the tiles alternate)
+  auto turn = [&](uint32_t t) { return bar0 + 8u * (9 + 4 * KS + t); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + FP::kMiscOff);
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + FP::kMiscOff + 4);
 
@@ -215,8 +262,10 @@ __global__ void __launch_bounds__(FmhaPlan<D>::kThreads, 1)
     }
     for (uint32_t t = 0; t < 2; ++t) {
       mbar_init(s_full(t), 1);
-      mbar_init(p_full(t), 4);  // one arrival per softmax warp of the tile
+      mbar_init(p_full(t, 0), 4);  // one arrival per softmax warp of the tile
+      mbar_init(p_full(t, 1), 4);
       mbar_init(o_done(t), 1);
+      mbar_init(turn(t), 4);  // one arrival per softmax warp of the other tile
     }
     *abort_flag = 0u;
     fence_mbarrier_init();
@@ -307,20 +356,26 @@ __global__ void __launch_bounds__(FmhaPlan<D>::kThreads, 1)
         if (!fmha_wait(v_full(s), ph, abort_flag, p, B2G_SITE_FULL)) break;
         const uint32_t v_base = sbase + FP::kVOff + s * FP::kTile;
         for (uint32_t t = 0; alive && t < n_tiles; ++t) {
-          if (!fmha_wait(p_full(t), static_cast<uint32_t>(j) & 1u, abort_flag, p,
-                         B2G_SITE_ACC_FULL)) {
-            alive = false;
-            break;
-          }
-          tc_fence_after();
           const uint32_t p_col = tmem_base + FP::kS + t * FP::kTileCols + FP::kP;
+          // P arrives in two 64-key halves; the first half's MMAs run while
+          // the softmax still computes the second
+          for (uint32_t half = 0; half < 2; ++half) {
+            if (!fmha_wait(p_full(t, half), static_cast<uint32_t>(j) & 1u, abort_flag, p,
+                           B2G_SITE_ACC_FULL)) {
+              alive = false;
+              break;
+            }
+            tc_fence_after();
 #pragma unroll
-          for (uint32_t kk = 0; kk < 128 / 16; ++kk) {
-            // 16 keys per MMA: two 8-row swizzle atoms; head-dim slabs are kRegion apart
-            const uint64_t bd = sdesc_mnmajor_sw128(v_base + kk * 2048u, FP::kRegion, 1024u);
-            mma_f16_ts(tmem_base + FP::kO + t * FP::kTileCols, p_col + kk * 8u, bd, idesc_pv,
-                       (j > 0 || kk > 0) ? 1u : 0u);
+            for (uint32_t k4 = 0; k4 < 4; ++k4) {
+              // 16 keys per MMA: two 8-row swizzle atoms; head-dim slabs are kRegion apart
+              const uint32_t kk = half * 4u + k4;
+              const uint64_t bd = sdesc_mnmajor_sw128(v_base + kk * 2048u, FP::kRegion, 1024u);
+              mma_f16_ts(tmem_base + FP::kO + t * FP::kTileCols, p_col + kk * 8u, bd, idesc_pv,
+                         (j > 0 || kk > 0) ? 1u : 0u);
+            }
           }
+          if (!alive) break;
           if (!has_next) {
             tc_commit<1>(o_done(t));
             last_bar = o_done(t);
@@ -390,13 +445,24 @@ __global__ void __launch_bounds__(FmhaPlan<D>::kThreads, 1)
           for (int c = 0; c < 128; ++c)
             if (c >= valid) s[c] = __float_as_uint(-INFINITY);
         }
-        float mx0 = __uint_as_float(s[0]), mx1 = __uint_as_float(s[1]);
+        // row max: eight independent chains of three-input maxima
+        float m8[8];
 #pragma unroll
-        for (int c = 2; c < 126; c += 4) {
-          mx0 = fmax3(mx0, __uint_as_float(s[c]), __uint_as_float(s[c + 1]));
-          mx1 = fmax3(mx1, __uint_as_float(s[c + 2]), __uint_as_float(s[c + 3]));
-        }
-        const float mx = fmax3(mx0, mx1, fmaxf(__uint_as_float(s[126]), __uint_as_float(s[127])));
+        for (int i = 0; i < 8; ++i) m8[i] = fmaxf(__uint_as_float(s[i]), __uint_as_float(s[i + 8]));
+#if B2G_FMHA_MAX3
+#pragma unroll
+        for (int c = 16; c < 128; c += 16)
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            m8[i] = fmax3(m8[i], __uint_as_float(s[c + i]), __uint_as_float(s[c + 8 + i]));
+#else
+#pragma unroll
+        for (int c = 16; c < 128; c += 8)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) m8[i] = fmaxf(m8[i], __uint_as_float(s[c + i]));
+#endif
+        const float mx = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]),
+                               fmaxf(m8[6], m8[7]));
         // The exponent offset moves only when the row max grows by more than
         // 2^kRescaleLog2 over it: P stays below 2^kRescaleLog2, the final 1/l
         // cancels the offset exactly, and most tiles skip the O rescale.
@@ -404,50 +470,78 @@ __global__ void __launch_bounds__(FmhaPlan<D>::kThreads, 1)
         const float m_cand = mx * sl2;
         const bool move = m_cand > m_run + kRescaleLog2;
         const float m_new = move ? m_cand : m_run;
-        const float alpha = move ? fast_exp2(m_run - m_new) : 1.0f;
+        // on the FMA pipe: the other tile may be holding the MUFU unit
+        float alpha = 1.0f;
+        if (move) alpha = poly_exp2(m_run - m_new);
 
-        float sum0 = 0.0f, sum1 = 0.0f;
+        // O holds PV_0..PV_{j-1} (the S_j commit follows them); rows whose
+        // offset moved are scaled by alpha before PV_j adds onto them
+        if (j >= 1 && __any_sync(0xffffffffu, move)) {
+#pragma unroll 1
+          for (uint32_t c0 = 0; c0 < static_cast<uint32_t>(D); c0 += 16u) {
+            uint32_t o[16];
+            tmem_ld_32x32b_x16(o_col + c0, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < 16; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+            tmem_st_32x32b_x16(o_col + c0, o);
+          }
+        }
+
+        // The two tiles' exponentials take turns (tile 0 first at each step), so
+        // each runs at the full MUFU rate while the tensor pipe works on the other
+        // tile; the turn is handed over a few pairs before the end.
+        const bool ordered = B2G_FMHA_ORDER != 0 && n_tiles == 2;
+        if (ordered && (t == 1 || j > 0)) {
+          const uint32_t ph = t == 0 ? (static_cast<uint32_t>(j - 1) & 1u) : (static_cast<uint32_t>(j) & 1u);
+          if (!__all_sync(0xffffffffu, fmha_wait(turn(t), ph, abort_flag, p, B2G_SITE_ACC_FULL))) {
+            alive = false;
+            break;
+          }
+        }
+        // P in two 64-key halves, each handed to the MMA as soon as it is in TMEM
+        const float2 sl2x2 = make_float2(sl2, sl2);
+        const float2 negm = make_float2(-m_new, -m_new);
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
           uint32_t pk[32];
 #pragma unroll
           for (int c = 0; c < 32; ++c) {
-            const float x0 = fmaf(__uint_as_float(s[half * 64 + 2 * c]), sl2, -m_new);
-            const float x1 = fmaf(__uint_as_float(s[half * 64 + 2 * c + 1]), sl2, -m_new);
-            float e0, e1;
+            const float2 sv = make_float2(__uint_as_float(s[half * 64 + 2 * c]),
+                                          __uint_as_float(s[half * 64 + 2 * c + 1]));
+            const float2 x = __ffma2_rn(sv, sl2x2, negm);
+            float2 e;
             if ((c & 3) < B2G_FMHA_POLY_PAIRS) {  // this share on the FMA pipe
-              e0 = poly_exp2(x0);
-              e1 = poly_exp2(x1);
+              e = poly_exp2x2(x);
             } else {
-              e0 = fast_exp2(x0);
-              e1 = fast_exp2(x1);
+              e.x = fast_exp2(x.x);
+              e.y = fast_exp2(x.y);
             }
-            sum0 += e0;
-            sum1 += e1;
-            pk[c] = pack2<kBF16>(e0, e1);
+            s[half * 64 + 2 * c] = __float_as_uint(e.x);
+            s[half * 64 + 2 * c + 1] = __float_as_uint(e.y);
+            pk[c] = pack2<kBF16>(e.x, e.y);
+            if (half == 1 && c == 32 - B2G_FMHA_TURN_EARLY && ordered) {
+              __syncwarp();
+              if (lane == 0) mbar_arrive(turn(t ^ 1u));
+            }
           }
           tmem_st_32x32b_x32(p_col + static_cast<uint32_t>(half) * 32u, pk);
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(p_full(t, static_cast<uint32_t>(half)));
         }
-        l_run = fmaf(l_run, alpha, sum0 + sum1);
+        // the row sum is off the critical path: P is already with the MMA
+        float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                         make_float2(0.f, 0.f)};
+#pragma unroll
+        for (int c = 0; c < 64; ++c)
+          acc[c & 3] = __fadd2_rn(acc[c & 3], make_float2(__uint_as_float(s[2 * c]),
+                                                          __uint_as_float(s[2 * c + 1])));
+        const float2 a01 = __fadd2_rn(acc[0], acc[1]), a23 = __fadd2_rn(acc[2], acc[3]);
+        const float2 a = __fadd2_rn(a01, a23);
+        l_run = fmaf(l_run, alpha, a.x + a.y);
         m_run = m_new;
-
-        // O holds PV_0..PV_{j-1} (the S_j commit follows them); rows whose
-        // offset moved are scaled by alpha before PV_j adds onto them
-        if (j >= 1 && __any_sync(0xffffffffu, move)) {
-#pragma unroll
-          for (uint32_t c0 = 0; c0 < static_cast<uint32_t>(D); c0 += 32u) {
-            uint32_t o[32];
-            tmem_ld_32x32b_x32(o_col + c0, o);
-            tmem_wait_ld();
-#pragma unroll
-            for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-            tmem_st_32x32b_x32(o_col + c0, o);
-          }
-        }
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(p_full(t));
       }
 
       if (alive && n_kv > 0 &&
