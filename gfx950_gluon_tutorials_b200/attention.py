@@ -166,3 +166,45 @@ def run_gluon_attention(q, k, v, o, metadata: MetaData, scale_on_q: bool = True)
     assert nheads_q % nheads_k == 0, "query heads must be a multiple of key/value heads"
     del scale_on_q  # the scale is always applied to the fp32 scores
     return attention_fwd(q, k, v, o, sm_scale=metadata.sm_scale, layout=metadata.layout)
+
+
+def main(argv=None) -> None:
+    """Times the forward pass on one problem, with the reference FMHA bench's
+    flags and defaults (kernels/attention/bench.py:103-155): seeded inputs,
+    CUDA-event timing on the current stream, TFLOPS from compute_flops."""
+    import argparse
+
+    ap = argparse.ArgumentParser(description="B200 FMHA forward timing")
+    ap.add_argument("--dtype", choices=["fp16", "bf16"], default="bf16")
+    ap.add_argument("--layout", choices=["bhsd", "bshd"], default="bhsd")
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--hq", type=int, default=64)
+    ap.add_argument("--hk", type=int, default=64)
+    ap.add_argument("--d", type=int, default=128)
+    ap.add_argument("--seqlen", type=int, default=8192)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--iters", type=int, default=10)
+    args = ap.parse_args(argv)
+    from .ops import check_status
+
+    dt = torch.bfloat16 if args.dtype == "bf16" else torch.float16
+    q, k, v, md = input_helper(args.batch, args.hq, args.hk, args.seqlen, args.seqlen, args.d, dt,
+                               args.layout)
+    o = torch.empty_like(q)
+    for _ in range(args.warmup):
+        run_gluon_attention(q, k, v, o, md)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.iters):
+        run_gluon_attention(q, k, v, o, md)
+    end.record()
+    torch.cuda.synchronize()
+    check_status()
+    ms = start.elapsed_time(end) / max(args.iters, 1)
+    flops = compute_flops(args.batch, args.hq, args.seqlen, args.seqlen, args.d, False)
+    print(f"FMHA B={args.batch} HQ={args.hq} HK={args.hk} S={args.seqlen} D={args.d} "
+          f"{args.dtype} {args.layout}: {ms * 1e3:.1f} us, {flops / ms / 1e9:.1f} TFLOPS")
+
+
+if __name__ == "__main__":
+    main()
