@@ -58,6 +58,11 @@
 #define B2G_FMHA_TURN_EARLY 4
 #endif
 
+// 1: exponentials in a second pass over 32-column chunks reloaded from TMEM.
+#ifndef B2G_FMHA_TWO_PASS
+#define B2G_FMHA_TWO_PASS 1
+#endif
+
 // 1: the row max uses three-input maxima.
 #ifndef B2G_FMHA_MAX3
 #define B2G_FMHA_MAX3 1
@@ -104,7 +109,12 @@ struct FmhaPlan {
   static constexpr uint32_t kDynBytes = kBytes + 1024;  // + alignment slack
   // TMEM columns: S_t = 128 t (128 fp32), P_t = S_t + 64 (128 x 16-bit),
   // O_t = 256 + 128 t (D fp32)
+#if B2G_FMHA_TWO_PASS
+  // P from column 0: each 16-column P chunk lands on scores already reloaded
+  static constexpr uint32_t kS = 0, kP = 0, kO = 256, kTileCols = 128;
+#else
   static constexpr uint32_t kS = 0, kP = 64, kO = 256, kTileCols = 128;
+#endif
   static_assert(D == 64 || D == 128, "head dim");
   static_assert(kDynBytes <= 232448, "shared memory");
 };
@@ -499,9 +509,56 @@ __global__ void __launch_bounds__(FmhaPlan<D>::kThreads, 1)
             break;
           }
         }
-        // P in two 64-key halves, each handed to the MMA as soon as it is in TMEM
         const float2 sl2x2 = make_float2(sl2, sl2);
         const float2 negm = make_float2(-m_new, -m_new);
+#if B2G_FMHA_TWO_PASS
+        // Second pass over the scores, 32 columns at a time from TMEM (the next
+        // chunk's load in flight while this one is exponentiated), so that few
+        // registers are live and many exponentials can be in flight. P chunk c
+        // (16 columns) overwrites score columns 16c.., already reloaded.
+        float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                         make_float2(0.f, 0.f)};
+        {
+          uint32_t buf[2][32];
+          tmem_ld_32x32b_x32(s_col, buf[0]);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            if (c < 3) tmem_ld_32x32b_x32(s_col + 32u * static_cast<uint32_t>(c + 1), buf[(c + 1) & 1]);
+            uint32_t (&cur)[32] = buf[c & 1];
+            if (valid < 128) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if (32 * c + i >= valid) cur[i] = __float_as_uint(-INFINITY);
+            }
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const float2 x = __ffma2_rn(make_float2(__uint_as_float(cur[2 * i]),
+                                                      __uint_as_float(cur[2 * i + 1])),
+                                          sl2x2, negm);
+              float2 e;
+              if ((i & 3) < B2G_FMHA_POLY_PAIRS) {
+                e = poly_exp2x2(x);
+              } else {
+                e.x = fast_exp2(x.x);
+                e.y = fast_exp2(x.y);
+              }
+              acc[i & 3] = __fadd2_rn(acc[i & 3], e);
+              pk[i] = pack2<kBF16>(e.x, e.y);
+            }
+            tmem_st_32x32b_x16(p_col + 16u * static_cast<uint32_t>(c), pk);
+            if (c == 1 || c == 3) {
+              tmem_wait_st();
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(p_full(t, static_cast<uint32_t>(c >> 1)));
+            }
+            if (c < 3) tmem_wait_ld();
+          }
+        }
+#else
+        // P in two 64-key halves, each handed to the MMA as soon as it is in TMEM
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
           uint32_t pk[32];
@@ -538,6 +595,7 @@ __global__ void __launch_bounds__(FmhaPlan<D>::kThreads, 1)
         for (int c = 0; c < 64; ++c)
           acc[c & 3] = __fadd2_rn(acc[c & 3], make_float2(__uint_as_float(s[2 * c]),
                                                           __uint_as_float(s[2 * c + 1])));
+#endif
         const float2 a01 = __fadd2_rn(acc[0], acc[1]), a23 = __fadd2_rn(acc[2], acc[3]);
         const float2 a = __fadd2_rn(a01, a23);
         l_run = fmaf(l_run, alpha, a.x + a.y);
