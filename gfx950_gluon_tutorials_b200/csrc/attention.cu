@@ -7,8 +7,9 @@
 // tile t and KV tile j of 128 keys:
 //   S_t  = Q_t K_j^T          tcgen05.mma into tile t's TMEM score buffer
 //   P_t  = exp2(S_t*s' - m)   softmax warpgroup t, one query row per thread; P is
-//                             stored back to TMEM as 16-bit values over the
-//                             upper half of S_t's columns
+//                             stored back to TMEM as 16-bit values over S_t's
+//                             columns (the first half with the two-pass softmax,
+//                             the upper half with the one-pass variant)
 //   O_t += P_t V_j            tcgen05.mma with A = P read from TMEM and B = V as an
 //                             MN-major shared-memory operand (no transpose pass)
 // The MMA thread interleaves the tiles (PV_0, S_0 next, PV_1, S_1 next, ...) so
@@ -87,7 +88,7 @@ struct alignas(64) FmhaParams {
 };
 
 // Shared memory and TMEM plan of one CTA: two 128-row query tiles (Q0, Q1),
-// K and V rings, and per tile one score buffer (P aliases its upper half once
+// K and V rings, and per tile one score buffer (P aliases half of it once
 // the scores are in registers) and one O accumulator.
 template <int D>
 struct FmhaPlan {
