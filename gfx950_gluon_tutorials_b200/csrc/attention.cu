@@ -723,6 +723,7 @@ extern "C" int b2g_attention_fwd(const void* q, const void* k, const void* v, vo
   }
   for (const void* ptr : {q, k, v, static_cast<const void*>(o)})
     if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0) return B2G_EALIGN;
+  if (reinterpret_cast<uintptr_t>(lse) % alignof(float) != 0) return B2G_EALIGN;
   if (current_device_sms() <= 0) return B2G_ENODEVICE;
   if (seqlen_q == 0) return B2G_OK;
 

@@ -169,6 +169,13 @@ def test_attention_argument_errors(kw, code):
     assert _call(**kw) == code
 
 
+def test_attention_lse_must_be_float_aligned():
+    arr = (ctypes.c_int64 * 16)(*([2 * 128 * 128, 128 * 128, 128, 1] * 4))
+    rc = _lib.lib().b2g_attention_fwd(4096, 8192, 12288, 16384, arr, 1, 2, 2, 128, 128, 128,
+                                      _lib.DT_BF16, 0.1, 4098, None, None)
+    assert rc == _lib.EALIGN
+
+
 def test_attention_strides_pointer_required():
     rc = _lib.lib().b2g_attention_fwd(4096, 8192, 12288, 16384, None, 1, 2, 2, 128, 128, 128,
                                       _lib.DT_BF16, 0.1, None, None, None)
