@@ -3,8 +3,8 @@
 // (kernels/attention/fmha_v4.py:343-758, launcher :761-790; torch oracle
 // kernels/attention/common.py:115-138 sdpa_reference).
 //
-// One CTA per (256 query rows = two 128-row tiles, query head, batch). Per
-// tile t and KV tile j of 128 keys:
+// Persistent: one CTA per SM loops over work items (256 query rows = two
+// 128-row tiles, query head, batch). Per tile t and KV tile j of 128 keys:
 //   S_t  = Q_t K_j^T          tcgen05.mma into tile t's TMEM score buffer
 //   P_t  = exp2(S_t*s' - m)   softmax warpgroup t, one query row per thread; P is
 //                             stored back to TMEM as 16-bit values over S_t's
@@ -48,27 +48,6 @@
 #define B2G_FMHA_POLY_PAIRS 0
 #endif
 
-// 1: the two tiles' softmax exponentials take strict turns on the MUFU unit.
-#ifndef B2G_FMHA_ORDER
-#define B2G_FMHA_ORDER 0
-#endif
-
-// Exponential pairs of a tile left when its softmax hands the MUFU turn to the
-// other tile (1..32).
-#ifndef B2G_FMHA_TURN_EARLY
-#define B2G_FMHA_TURN_EARLY 4
-#endif
-
-// 1: exponentials in a second pass over 32-column chunks reloaded from TMEM.
-#ifndef B2G_FMHA_TWO_PASS
-#define B2G_FMHA_TWO_PASS 1
-#endif
-
-// 1: the row max uses three-input maxima.
-#ifndef B2G_FMHA_MAX3
-#define B2G_FMHA_MAX3 1
-#endif
-
 // Suspend-time hint of the slow path of the bounded waits (0: plain probes).
 #ifndef B2G_FMHA_WAIT_HINT_NS
 #define B2G_FMHA_WAIT_HINT_NS 20000
@@ -82,7 +61,7 @@ struct alignas(64) FmhaParams {
   int64_t o_sb, o_sh, o_ss;   // element strides of O (d contiguous)
   float* lse;                 // [B][HQ][S_q] natural-log log-sum-exp, or null
   int* status;
-  int32_t HQ, HK, S_q, S_k;
+  int32_t B, HQ, HK, S_q, S_k;
   float scale_log2;           // sm_scale * log2(e)
   uint64_t timeout_ns;
 };
@@ -103,19 +82,15 @@ struct FmhaPlan {
   static constexpr uint32_t kVOff = kKOff + kStages * kTile;
   static constexpr uint32_t kBarOff = kVOff + kStages * kTile;
   // q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_full[2][2]
-  // (tile, key half), o_done[2], turn[2]
-  static constexpr uint32_t kNumBars = 1 + 4 * kStages + 10;
+  // (tile, key half), o_done[2], q_empty, o_free[2]
+  static constexpr uint32_t kNumBars = 1 + 4 * kStages + 11;
   static constexpr uint32_t kMiscOff = kBarOff + kNumBars * 8;  // tmem slot, abort flag
   static constexpr uint32_t kBytes = kMiscOff + 16;
   static constexpr uint32_t kDynBytes = kBytes + 1024;  // + alignment slack
   // TMEM columns: S_t = 128 t (128 fp32), P_t = S_t + 64 (128 x 16-bit),
   // O_t = 256 + 128 t (D fp32)
-#if B2G_FMHA_TWO_PASS
   // P from column 0: each 16-column P chunk lands on scores already reloaded
   static constexpr uint32_t kS = 0, kP = 0, kO = 256, kTileCols = 128;
-#else
-  static constexpr uint32_t kS = 0, kP = 64, kO = 256, kTileCols = 128;
-#endif
   static_assert(D == 64 || D == 128, "head dim");
   static_assert(kDynBytes <= 232448, "shared memory");
 };
@@ -242,12 +217,24 @@ __global__ void __launch_bounds__(FmhaPlan<D>::kThreads, 1)
                                              ~static_cast<uintptr_t>(1023));
   const uint32_t sbase = smem_u32(smem);
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int32_t m0 = static_cast<int32_t>(blockIdx.x) * 256;
-  const int32_t h = static_cast<int32_t>(blockIdx.y);
-  const int32_t b = static_cast<int32_t>(blockIdx.z);
-  const int32_t hk = h / (p.HQ / p.HK);
   const int32_t n_kv = (p.S_k + 127) / 128;
-  const uint32_t n_tiles = p.S_q - m0 > 128 ? 2u : 1u;  // query tiles holding rows
+  // Persistent: work items are (256-row query block, query head, batch), the
+  // query block fastest, so the CTAs working at one time share K and V in L2.
+  const int32_t n_mblk = (p.S_q + 255) / 256;
+  const int32_t n_items = n_mblk * p.HQ * p.B;
+  struct Item {
+    int32_t m0, h, b, hk;
+    uint32_t tiles;  // query tiles holding rows (1 or 2)
+  };
+  auto item_at = [&](int32_t it) {
+    Item w;
+    w.m0 = (it % n_mblk) * 256;
+    w.h = (it / n_mblk) % p.HQ;
+    w.b = it / (n_mblk * p.HQ);
+    w.hk = w.h / (p.HQ / p.HK);
+    w.tiles = p.S_q - w.m0 > 128 ? 2u : 1u;
+    return w;
+  };
 
   const uint32_t bar0 = sbase + FP::kBarOff;
   const uint32_t q_full = bar0;
@@ -258,13 +245,16 @@ __global__ void __launch_bounds__(FmhaPlan<D>::kThreads, 1)
   auto s_full = [&](uint32_t t) { return bar0 + 8u * (1 + 4 * KS + t); };
   auto p_full = [&](uint32_t t, uint32_t half) { return bar0 + 8u * (3 + 4 * KS + 2 * t + half); };
   auto o_done = [&](uint32_t t) { return bar0 + 8u * (7 + 4 * KS + t); };
-  // turn(t): tile t's softmax may start its exponentials (the tiles alternate)
-  auto turn = [&](uint32_t t) { return bar0 + 8u * (9 + 4 * KS + t); };
+  // q_empty: the item's last S MMAs are done with Q; o_free(t): the epilogue
+  // has read tile t's O, so the next item's first PV may overwrite it
+  const uint32_t q_empty = bar0 + 8u * (9 + 4 * KS);
+  auto o_free = [&](uint32_t t) { return bar0 + 8u * (10 + 4 * KS + t); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + FP::kMiscOff);
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + FP::kMiscOff + 4);
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (uint32_t s = 0; s < KS; ++s) {
       mbar_init(k_full(s), 1);
       mbar_init(k_empty(s), 1);
@@ -276,7 +266,7 @@ __global__ void __launch_bounds__(FmhaPlan<D>::kThreads, 1)
       mbar_init(p_full(t, 0), 4);  // one arrival per softmax warp of the tile
       mbar_init(p_full(t, 1), 4);
       mbar_init(o_done(t), 1);
-      mbar_init(turn(t), 4);  // one arrival per softmax warp of the other tile
+      mbar_init(o_free(t), 4);
     }
     *abort_flag = 0u;
     fence_mbarrier_init();
@@ -295,35 +285,55 @@ __global__ void __launch_bounds__(FmhaPlan<D>::kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer --
+    // Q once per item (after the previous item's last S is done with it); K
+    // and V through the rings, whose step count runs on across items.
     if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, n_tiles * FP::kTile);
-      for (uint32_t t = 0; t < n_tiles; ++t)
-        for (uint32_t r = 0; r < FP::kRegions; ++r)
-          tma_load_4d(sbase + FP::kQOff + t * FP::kTile + r * FP::kRegion, &p.tmQ, q_full,
-                      r * 64, m0 + static_cast<int32_t>(t) * 128, h, b);
-      int32_t j = 0;
-      for (; j < n_kv; ++j) {
-        const uint32_t s = static_cast<uint32_t>(j) % KS, ph = (static_cast<uint32_t>(j) / KS) & 1u;
-        if (!fmha_wait(k_empty(s), ph ^ 1u, abort_flag, p, B2G_SITE_EMPTY)) break;
-        mbar_arrive_expect_tx(k_full(s), FP::kTile);
-        for (uint32_t r = 0; r < FP::kRegions; ++r)
-          tma_load_4d(sbase + FP::kKOff + s * FP::kTile + r * FP::kRegion, &p.tmK, k_full(s),
-                      r * 64, j * 128, hk, b);
-        if (!fmha_wait(v_empty(s), ph ^ 1u, abort_flag, p, B2G_SITE_EMPTY)) break;
-        mbar_arrive_expect_tx(v_full(s), FP::kTile);
-        for (uint32_t r = 0; r < FP::kRegions; ++r)
-          tma_load_4d(sbase + FP::kVOff + s * FP::kTile + r * FP::kRegion, &p.tmV, v_full(s),
-                      r * 64, j * 128, hk, b);
+      uint32_t jg = 0, ic = 0;  // K/V steps and items issued
+      uint32_t nk = 0, nv = 0;  // K and V loads issued
+      bool alive = true;
+      for (int32_t item = static_cast<int32_t>(blockIdx.x); alive && item < n_items;
+           item += static_cast<int32_t>(gridDim.x), ++ic) {
+        const Item w = item_at(item);
+        if (ic > 0 && !fmha_wait(q_empty, (ic - 1u) & 1u, abort_flag, p, B2G_SITE_EMPTY)) break;
+        mbar_arrive_expect_tx(q_full, w.tiles * FP::kTile);
+        for (uint32_t t = 0; t < w.tiles; ++t)
+          for (uint32_t r = 0; r < FP::kRegions; ++r)
+            tma_load_4d(sbase + FP::kQOff + t * FP::kTile + r * FP::kRegion, &p.tmQ, q_full,
+                        r * 64, w.m0 + static_cast<int32_t>(t) * 128, w.h, w.b);
+        for (int32_t j = 0; j < n_kv; ++j, ++jg) {
+          const uint32_t s = jg % KS, ph = (jg / KS) & 1u;
+          if (!fmha_wait(k_empty(s), ph ^ 1u, abort_flag, p, B2G_SITE_EMPTY)) {
+            alive = false;
+            break;
+          }
+          mbar_arrive_expect_tx(k_full(s), FP::kTile);
+          for (uint32_t r = 0; r < FP::kRegions; ++r)
+            tma_load_4d(sbase + FP::kKOff + s * FP::kTile + r * FP::kRegion, &p.tmK, k_full(s),
+                        r * 64, j * 128, w.hk, w.b);
+          ++nk;
+          if (!fmha_wait(v_empty(s), ph ^ 1u, abort_flag, p, B2G_SITE_EMPTY)) {
+            alive = false;
+            break;
+          }
+          mbar_arrive_expect_tx(v_full(s), FP::kTile);
+          for (uint32_t r = 0; r < FP::kRegions; ++r)
+            tma_load_4d(sbase + FP::kVOff + s * FP::kTile + r * FP::kRegion, &p.tmV, v_full(s),
+                        r * 64, j * 128, w.hk, w.b);
+          ++nv;
+        }
       }
-      // every load issued lands before the CTA can exit
+      // every load issued lands before the CTA can exit: the last Q and the
+      // K and V loads of the last KS steps (older ones were consumed)
       uint32_t spins = 0;
-      while (!mbar_try_wait(q_full, 0) && spins < (1u << 20)) ++spins;
-      for (int32_t i = j > static_cast<int32_t>(KS) ? j - static_cast<int32_t>(KS) : 0; i < j; ++i) {
-        const uint32_t s = static_cast<uint32_t>(i) % KS, ph = (static_cast<uint32_t>(i) / KS) & 1u;
+      if (ic > 0)
+        while (!mbar_try_wait(q_full, (ic - 1u) & 1u) && spins < (1u << 20)) ++spins;
+      for (uint32_t i = nk > KS ? nk - KS : 0u; i < nk; ++i) {
         spins = 0;
-        while (!mbar_try_wait(k_full(s), ph) && spins < (1u << 20)) ++spins;
+        while (!mbar_try_wait(k_full(i % KS), (i / KS) & 1u) && spins < (1u << 20)) ++spins;
+      }
+      for (uint32_t i = nv > KS ? nv - KS : 0u; i < nv; ++i) {
         spins = 0;
-        while (!mbar_try_wait(v_full(s), ph) && spins < (1u << 20)) ++spins;
+        while (!mbar_try_wait(v_full(i % KS), (i / KS) & 1u) && spins < (1u << 20)) ++spins;
       }
     }
   } else if (warp == 1) {
@@ -332,6 +342,8 @@ __global__ void __launch_bounds__(FmhaPlan<D>::kThreads, 1)
     // columns, and the tensor pipe runs one thread's MMAs in issue order, so
     // S_{j+1} is issued only after PV_j. The two tiles interleave: while one
     // tile's softmax runs, the other tile's PV and next S keep the pipe busy.
+    // Across items, the next item's first S and softmax overlap this item's
+    // epilogue; only its first PV waits for the O columns to be read out.
     if (lane == 0) {
       constexpr uint32_t idesc_s = fmha_idesc_s<D, kBF16>();
       constexpr uint32_t idesc_pv = fmha_idesc_pv<D, kBF16>();
@@ -347,65 +359,84 @@ __global__ void __launch_bounds__(FmhaPlan<D>::kThreads, 1)
           mma_f16<1>(tmem_base + FP::kS + t * FP::kTileCols, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
         }
       };
-      bool alive = fmha_wait(q_full, 0, abort_flag, p, B2G_SITE_FULL) &&
-                   fmha_wait(k_full(0), 0, abort_flag, p, B2G_SITE_FULL);
-      if (alive) {
+      uint32_t jg = 0, ic = 0;             // K/V steps and items
+      uint32_t steps[2] = {0u, 0u};        // steps of each tile (phases of s_full, p_full)
+      uint32_t titems[2] = {0u, 0u};       // items of each tile (phases of o_done, o_free)
+      bool alive = true;
+      for (int32_t item = static_cast<int32_t>(blockIdx.x); alive && item < n_items;
+           item += static_cast<int32_t>(gridDim.x), ++ic) {
+        const Item w = item_at(item);
+        const uint32_t nt = w.tiles;
+        if (!fmha_wait(q_full, ic & 1u, abort_flag, p, B2G_SITE_FULL) ||
+            !fmha_wait(k_full(jg % KS), (jg / KS) & 1u, abort_flag, p, B2G_SITE_FULL))
+          break;
         tc_fence_after();
-        for (uint32_t t = 0; t < n_tiles; ++t) {
-          issue_s(t, 0);
+        for (uint32_t t = 0; t < nt; ++t) {
+          issue_s(t, jg % KS);
           tc_commit<1>(s_full(t));
         }
-        tc_commit<1>(k_empty(0));
-        last_bar = k_empty(0);
-        last_par = 0;
-      }
-      for (int32_t j = 0; alive && j < n_kv; ++j) {
-        const uint32_t s = static_cast<uint32_t>(j) % KS, ph = (static_cast<uint32_t>(j) / KS) & 1u;
-        const bool has_next = j + 1 < n_kv;
-        const uint32_t s1 = static_cast<uint32_t>(j + 1) % KS;
-        const uint32_t ph1 = (static_cast<uint32_t>(j + 1) / KS) & 1u;
-        if (!fmha_wait(v_full(s), ph, abort_flag, p, B2G_SITE_FULL)) break;
-        const uint32_t v_base = sbase + FP::kVOff + s * FP::kTile;
-        for (uint32_t t = 0; alive && t < n_tiles; ++t) {
-          const uint32_t p_col = tmem_base + FP::kS + t * FP::kTileCols + FP::kP;
-          // P arrives in two 64-key halves; the first half's MMAs run while
-          // the softmax still computes the second
-          for (uint32_t half = 0; half < 2; ++half) {
-            if (!fmha_wait(p_full(t, half), static_cast<uint32_t>(j) & 1u, abort_flag, p,
-                           B2G_SITE_ACC_FULL)) {
+        last_bar = s_full(0);
+        last_par = steps[0] & 1u;
+        if (n_kv == 1) tc_commit<1>(q_empty);  // the item's last S MMAs are issued
+        tc_commit<1>(k_empty(jg % KS));
+        for (int32_t j = 0; j < n_kv; ++j, ++jg) {
+          const uint32_t s = jg % KS, ph = (jg / KS) & 1u;
+          const bool has_next = j + 1 < n_kv;
+          const uint32_t s1 = (jg + 1) % KS, ph1 = ((jg + 1) / KS) & 1u;
+          if (!fmha_wait(v_full(s), ph, abort_flag, p, B2G_SITE_FULL)) {
+            alive = false;
+            break;
+          }
+          const uint32_t v_base = sbase + FP::kVOff + s * FP::kTile;
+          for (uint32_t t = 0; alive && t < nt; ++t) {
+            const uint32_t p_col = tmem_base + FP::kS + t * FP::kTileCols + FP::kP;
+            // the previous item's epilogue must have read this tile's O
+            if (j == 0 && titems[t] > 0 &&
+                !fmha_wait(o_free(t), (titems[t] - 1u) & 1u, abort_flag, p, B2G_SITE_ACC_EMPTY)) {
+              alive = false;
+              break;
+            }
+            // P arrives in two 64-key halves; the first half's MMAs run while
+            // the softmax still computes the second
+            for (uint32_t half = 0; half < 2; ++half) {
+              if (!fmha_wait(p_full(t, half), steps[t] & 1u, abort_flag, p, B2G_SITE_ACC_FULL)) {
+                alive = false;
+                break;
+              }
+              tc_fence_after();
+#pragma unroll
+              for (uint32_t k4 = 0; k4 < 4; ++k4) {
+                // 16 keys per MMA: two 8-row swizzle atoms; head-dim slabs are kRegion apart
+                const uint32_t kk = half * 4u + k4;
+                const uint64_t bd = sdesc_mnmajor_sw128(v_base + kk * 2048u, FP::kRegion, 1024u);
+                mma_f16_ts(tmem_base + FP::kO + t * FP::kTileCols, p_col + kk * 8u, bd, idesc_pv,
+                           (j > 0 || kk > 0) ? 1u : 0u);
+              }
+            }
+            if (!alive) break;
+            ++steps[t];
+            if (!has_next) {
+              tc_commit<1>(o_done(t));
+              last_bar = o_done(t);
+              last_par = titems[t] & 1u;
+              ++titems[t];
+              continue;
+            }
+            if (t == 0 && !fmha_wait(k_full(s1), ph1, abort_flag, p, B2G_SITE_FULL)) {
               alive = false;
               break;
             }
             tc_fence_after();
-#pragma unroll
-            for (uint32_t k4 = 0; k4 < 4; ++k4) {
-              // 16 keys per MMA: two 8-row swizzle atoms; head-dim slabs are kRegion apart
-              const uint32_t kk = half * 4u + k4;
-              const uint64_t bd = sdesc_mnmajor_sw128(v_base + kk * 2048u, FP::kRegion, 1024u);
-              mma_f16_ts(tmem_base + FP::kO + t * FP::kTileCols, p_col + kk * 8u, bd, idesc_pv,
-                         (j > 0 || kk > 0) ? 1u : 0u);
-            }
+            issue_s(t, s1);
+            tc_commit<1>(s_full(t));
+            last_bar = s_full(t);
+            last_par = steps[t] & 1u;
           }
           if (!alive) break;
-          if (!has_next) {
-            tc_commit<1>(o_done(t));
-            last_bar = o_done(t);
-            last_par = 0;
-            continue;
-          }
-          if (t == 0 && !fmha_wait(k_full(s1), ph1, abort_flag, p, B2G_SITE_FULL)) {
-            alive = false;
-            break;
-          }
-          tc_fence_after();
-          issue_s(t, s1);
-          tc_commit<1>(s_full(t));
-          last_bar = s_full(t);
-          last_par = static_cast<uint32_t>(j + 1) & 1u;
+          if (j + 2 == n_kv) tc_commit<1>(q_empty);  // the item's last S MMAs are issued
+          tc_commit<1>(v_empty(s));
+          if (has_next) tc_commit<1>(k_empty(s1));
         }
-        if (!alive) break;
-        tc_commit<1>(v_empty(s));
-        if (has_next) tc_commit<1>(k_empty(s1));
       }
       // all MMAs issued by this thread finish before TMEM can be freed
       if (last_bar != 0u) {
@@ -419,7 +450,7 @@ __global__ void __launch_bounds__(FmhaPlan<D>::kThreads, 1)
     // owns row 32 * (w % 4) + i of it: the TMEM lane quarter a warp may touch
     // is fixed by its index in the warpgroup.
     const uint32_t t = (warp - 2u) >> 2;
-    if (t < n_tiles) {
+    {
       const uint32_t quarter = warp & 3u;
       const uint32_t row = quarter * 32u + lane;
       const uint32_t taddr = tmem_base + ((quarter * 32u) << 16);
@@ -427,11 +458,16 @@ __global__ void __launch_bounds__(FmhaPlan<D>::kThreads, 1)
       const uint32_t p_col = s_col + FP::kP;
       const uint32_t o_col = taddr + FP::kO + t * FP::kTileCols;
       const float sl2 = p.scale_log2;
+      uint32_t step = 0, ti = 0;  // this tile's steps and items (barrier phases)
+      bool alive = true;
+      for (int32_t item = static_cast<int32_t>(blockIdx.x); alive && item < n_items;
+           item += static_cast<int32_t>(gridDim.x)) {
+      const Item w = item_at(item);
+      if (t >= w.tiles) continue;
       float m_run = -INFINITY;  // exponent offset, log2 units (a running max of s * sl2)
       float l_run = 0.0f;       // running sum of exp2(s * sl2 - m_run)
-      bool alive = true;
-      for (int32_t j = 0; j < n_kv; ++j) {
-        if (!__all_sync(0xffffffffu, fmha_wait(s_full(t), static_cast<uint32_t>(j) & 1u,
+      for (int32_t j = 0; j < n_kv; ++j, ++step) {
+        if (!__all_sync(0xffffffffu, fmha_wait(s_full(t), step & 1u,
                                                abort_flag, p, B2G_SITE_ACC_FULL))) {
           alive = false;
           break;
@@ -460,18 +496,11 @@ __global__ void __launch_bounds__(FmhaPlan<D>::kThreads, 1)
         float m8[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) m8[i] = fmaxf(__uint_as_float(s[i]), __uint_as_float(s[i + 8]));
-#if B2G_FMHA_MAX3
 #pragma unroll
         for (int c = 16; c < 128; c += 16)
 #pragma unroll
           for (int i = 0; i < 8; ++i)
             m8[i] = fmax3(m8[i], __uint_as_float(s[c + i]), __uint_as_float(s[c + 8 + i]));
-#else
-#pragma unroll
-        for (int c = 16; c < 128; c += 8)
-#pragma unroll
-          for (int i = 0; i < 8; ++i) m8[i] = fmaxf(m8[i], __uint_as_float(s[c + i]));
-#endif
         const float mx = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]),
                                fmaxf(m8[6], m8[7]));
         // The exponent offset moves only when the row max grows by more than
@@ -499,20 +528,8 @@ __global__ void __launch_bounds__(FmhaPlan<D>::kThreads, 1)
           }
         }
 
-        // The two tiles' exponentials take turns (tile 0 first at each step), so
-        // each runs at the full MUFU rate while the tensor pipe works on the other
-        // tile; the turn is handed over a few pairs before the end.
-        const bool ordered = B2G_FMHA_ORDER != 0 && n_tiles == 2;
-        if (ordered && (t == 1 || j > 0)) {
-          const uint32_t ph = t == 0 ? (static_cast<uint32_t>(j - 1) & 1u) : (static_cast<uint32_t>(j) & 1u);
-          if (!__all_sync(0xffffffffu, fmha_wait(turn(t), ph, abort_flag, p, B2G_SITE_ACC_FULL))) {
-            alive = false;
-            break;
-          }
-        }
         const float2 sl2x2 = make_float2(sl2, sl2);
         const float2 negm = make_float2(-m_new, -m_new);
-#if B2G_FMHA_TWO_PASS
         // Second pass over the scores, 32 columns at a time from TMEM (the next
         // chunk's load in flight while this one is exponentiated), so that few
         // registers are live and many exponentials can be in flight. P chunk c
@@ -558,83 +575,52 @@ __global__ void __launch_bounds__(FmhaPlan<D>::kThreads, 1)
             if (c < 3) tmem_wait_ld();
           }
         }
-#else
-        // P in two 64-key halves, each handed to the MMA as soon as it is in TMEM
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t pk[32];
-#pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            const float2 sv = make_float2(__uint_as_float(s[half * 64 + 2 * c]),
-                                          __uint_as_float(s[half * 64 + 2 * c + 1]));
-            const float2 x = __ffma2_rn(sv, sl2x2, negm);
-            float2 e;
-            if ((c & 3) < B2G_FMHA_POLY_PAIRS) {  // this share on the FMA pipe
-              e = poly_exp2x2(x);
-            } else {
-              e.x = fast_exp2(x.x);
-              e.y = fast_exp2(x.y);
-            }
-            s[half * 64 + 2 * c] = __float_as_uint(e.x);
-            s[half * 64 + 2 * c + 1] = __float_as_uint(e.y);
-            pk[c] = pack2<kBF16>(e.x, e.y);
-            if (half == 1 && c == 32 - B2G_FMHA_TURN_EARLY && ordered) {
-              __syncwarp();
-              if (lane == 0) mbar_arrive(turn(t ^ 1u));
-            }
-          }
-          tmem_st_32x32b_x32(p_col + static_cast<uint32_t>(half) * 32u, pk);
-          tmem_wait_st();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(p_full(t, static_cast<uint32_t>(half)));
-        }
-        // the row sum is off the critical path: P is already with the MMA
-        float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
-                         make_float2(0.f, 0.f)};
-#pragma unroll
-        for (int c = 0; c < 64; ++c)
-          acc[c & 3] = __fadd2_rn(acc[c & 3], make_float2(__uint_as_float(s[2 * c]),
-                                                          __uint_as_float(s[2 * c + 1])));
-#endif
         const float2 a01 = __fadd2_rn(acc[0], acc[1]), a23 = __fadd2_rn(acc[2], acc[3]);
         const float2 a = __fadd2_rn(a01, a23);
         l_run = fmaf(l_run, alpha, a.x + a.y);
         m_run = m_new;
       }
 
-      if (alive && n_kv > 0 &&
-          __all_sync(0xffffffffu, fmha_wait(o_done(t), 0, abort_flag, p, B2G_SITE_ACC_FULL))) {
-        tc_fence_after();
-        const int32_t q_row = m0 + static_cast<int32_t>(t * 128u + row);
-        const bool in_range = q_row < p.S_q;
+      if (!alive) break;
+      // epilogue: O into registers, the columns released to the next item's
+      // first PV, then the scaled rows stored
+      if (!__all_sync(0xffffffffu, fmha_wait(o_done(t), ti & 1u, abort_flag, p, B2G_SITE_ACC_FULL))) {
+        alive = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t o[D];
+#pragma unroll
+      for (uint32_t c0 = 0; c0 < static_cast<uint32_t>(D); c0 += 32u)
+        tmem_ld_32x32b_x32(o_col + c0, *reinterpret_cast<uint32_t(*)[32]>(&o[c0]));
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(o_free(t));
+      ++ti;
+      const int32_t q_row = w.m0 + static_cast<int32_t>(t * 128u + row);
+      if (q_row < p.S_q) {
         const float inv_l = 1.0f / l_run;
         using OutT = typename std::conditional<kBF16, __nv_bfloat16, __half>::type;
-        OutT* orow = static_cast<OutT*>(p.O) + static_cast<int64_t>(b) * p.o_sb +
-                     static_cast<int64_t>(h) * p.o_sh + static_cast<int64_t>(q_row) * p.o_ss;
+        OutT* orow = static_cast<OutT*>(p.O) + static_cast<int64_t>(w.b) * p.o_sb +
+                     static_cast<int64_t>(w.h) * p.o_sh + static_cast<int64_t>(q_row) * p.o_ss;
+        uint4* dst = reinterpret_cast<uint4*>(orow);
 #pragma unroll
-        for (uint32_t c0 = 0; c0 < static_cast<uint32_t>(D); c0 += 32u) {
-          uint32_t o[32];
-          tmem_ld_32x32b_x32(o_col + c0, o);
-          tmem_wait_ld();
-          if (in_range) {
-            uint4* dst = reinterpret_cast<uint4*>(orow + c0);
-#pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              uint4 w;
-              w.x = pack2<kBF16>(__uint_as_float(o[8 * v + 0]) * inv_l, __uint_as_float(o[8 * v + 1]) * inv_l);
-              w.y = pack2<kBF16>(__uint_as_float(o[8 * v + 2]) * inv_l, __uint_as_float(o[8 * v + 3]) * inv_l);
-              w.z = pack2<kBF16>(__uint_as_float(o[8 * v + 4]) * inv_l, __uint_as_float(o[8 * v + 5]) * inv_l);
-              w.w = pack2<kBF16>(__uint_as_float(o[8 * v + 6]) * inv_l, __uint_as_float(o[8 * v + 7]) * inv_l);
-              dst[v] = w;
-            }
-          }
+        for (int v = 0; v < D / 8; ++v) {
+          uint4 u;
+          u.x = pack2<kBF16>(__uint_as_float(o[8 * v + 0]) * inv_l, __uint_as_float(o[8 * v + 1]) * inv_l);
+          u.y = pack2<kBF16>(__uint_as_float(o[8 * v + 2]) * inv_l, __uint_as_float(o[8 * v + 3]) * inv_l);
+          u.z = pack2<kBF16>(__uint_as_float(o[8 * v + 4]) * inv_l, __uint_as_float(o[8 * v + 5]) * inv_l);
+          u.w = pack2<kBF16>(__uint_as_float(o[8 * v + 6]) * inv_l, __uint_as_float(o[8 * v + 7]) * inv_l);
+          dst[v] = u;
         }
-        if (in_range && p.lse != nullptr) {
+        if (p.lse != nullptr) {
           // natural-log log-sum-exp of the scaled scores of this row
           constexpr float kLn2 = 0.693147180559945309f;
-          p.lse[(static_cast<int64_t>(b) * p.HQ + h) * p.S_q + q_row] = (m_run + __log2f(l_run)) * kLn2;
+          p.lse[(static_cast<int64_t>(w.b) * p.HQ + w.h) * p.S_q + q_row] =
+              (m_run + __log2f(l_run)) * kLn2;
         }
+      }
       }
     }
   }
@@ -688,8 +674,12 @@ int launch_fmha(const FmhaParams& prm, int batch, int heads_q, int seqlen_q, cud
       return static_cast<int>(cudaGetLastError());
     attr_set[dev].store(true);
   }
-  const dim3 grid(static_cast<unsigned>((seqlen_q + 255) / 256), static_cast<unsigned>(heads_q),
-                  static_cast<unsigned>(batch));
+  // persistent: one CTA per SM, looping over the (query block, head, batch) items
+  const int64_t items = static_cast<int64_t>((seqlen_q + 255) / 256) * heads_q * batch;
+  const int sms = current_device_sms();
+  if (sms <= 0) return B2G_ENODEVICE;
+  if (items > INT32_MAX) return B2G_ESHAPE;
+  const dim3 grid(static_cast<unsigned>(items < sms ? items : sms), 1, 1);
   kern<<<grid, FP::kThreads, dyn, stream>>>(prm);
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? B2G_OK : static_cast<int>(e);
@@ -739,6 +729,7 @@ extern "C" int b2g_attention_fwd(const void* q, const void* k, const void* v, vo
   prm.o_ss = strides[14];
   prm.lse = lse;
   prm.status = status;
+  prm.B = batch;
   prm.HQ = heads_q;
   prm.HK = heads_k;
   prm.S_q = seqlen_q;
