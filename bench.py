@@ -144,7 +144,7 @@ class ClockSampler:
                 "samples": len(sel), "reasons": reasons}
 
 
-def dist_setup(n_gpus: int):
+def dist_setup(n_gpus: int, cuda: bool = True):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -154,7 +154,7 @@ def dist_setup(n_gpus: int):
         torch.distributed.init_process_group(
             "nccl", timeout=datetime.timedelta(seconds=120),
             device_id=torch.device("cuda", local))
-    else:
+    elif cuda:
         torch.cuda.set_device(0)
     if world != n_gpus and rank == 0:
         log(f"note: --gpus {n_gpus} but WORLD_SIZE={world}; using {world}")
@@ -519,7 +519,8 @@ def read_traffic(kernel_key: str):
 
 # ---------------------------------------------------------------- contract --
 def contract_main(args):
-    rank, world, local = dist_setup(args.gpus)
+    # the reference arm times a CPU path: a single process needs no GPU
+    rank, world, local = dist_setup(args.gpus, cuda=args.impl != "reference")
     if args.impl == "reference":
         return reference_main(args, rank, world)
     import gfx950_gluon_tutorials_b200 as pkg
