@@ -86,6 +86,21 @@ def test_matches_oracle(cuda_device, shape, layout, dtype):
     np.testing.assert_allclose(lse.cpu().numpy(), lse_ref, rtol=1e-4, atol=1e-4)
 
 
+@pytest.mark.parametrize("dtype", ["float16", "bfloat16"])
+def test_many_items_with_mixed_tile_counts(cuda_device, dtype):
+    """More work items than SMs, where every other item holds one query tile
+    (Sq = 300 = 256 + 44): the persistent CTAs' per-tile barrier phases must
+    stay in step across items of both kinds."""
+    shape = (2, 100, 20, 300, 200, 64)
+    B, HQ, HK, Sq, Sk, D = shape
+    q, k, v = _inputs(*shape, TDT[dtype], "bshd", seed=123)
+    o, lse = _run(q, k, v, "bshd", D ** -0.5, with_lse=True)
+    o_ref, lse_ref = _oracle(q, k, v, "bshd", D ** -0.5)
+    ok, mx, mean = oa.check_output(_to_bhsd(o, "bshd").float().cpu().numpy(), o_ref, dtype)
+    assert ok, f"max |diff| {mx:.3e}, mean {mean:.3e}"
+    np.testing.assert_allclose(lse.cpu().numpy(), lse_ref, rtol=1e-4, atol=1e-4)
+
+
 def test_large_scores_and_moving_max(cuda_device):
     """Scores spread over hundreds of units in log2: the running max moves
     often and by large steps, exercising the O rescale; rows where a late key
