@@ -530,21 +530,28 @@ __global__ void __launch_bounds__(FmhaPlan<D>::kThreads, 1)
 
         const float2 sl2x2 = make_float2(sl2, sl2);
         const float2 negm = make_float2(-m_new, -m_new);
-        // Second pass over the scores, 32 columns at a time from TMEM (the next
-        // chunk's load in flight while this one is exponentiated), so that few
+        // Exponentials, 32 columns at a time: chunks 0 and 1 straight from the
+        // registers of the max pass, chunks 2 and 3 reloaded from TMEM (each load
+        // in flight while the previous chunk is exponentiated), so that few
         // registers are live and many exponentials can be in flight. P chunk c
-        // (16 columns) overwrites score columns 16c.., already reloaded.
+        // (16 columns) overwrites score columns 16c.., whose scores are in
+        // registers already.
         float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                          make_float2(0.f, 0.f)};
         {
           uint32_t buf[2][32];
-          tmem_ld_32x32b_x32(s_col, buf[0]);
-          tmem_wait_ld();
+          tmem_ld_32x32b_x32(s_col + 64u, buf[0]);
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
-            if (c < 3) tmem_ld_32x32b_x32(s_col + 32u * static_cast<uint32_t>(c + 1), buf[(c + 1) & 1]);
-            uint32_t (&cur)[32] = buf[c & 1];
-            if (valid < 128) {
+            if (c == 2) {
+              tmem_wait_ld();
+              tmem_ld_32x32b_x32(s_col + 96u, buf[1]);
+            }
+            if (c == 3) tmem_wait_ld();
+            uint32_t cur[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) cur[i] = c < 2 ? s[32 * c + i] : buf[c - 2][i];
+            if (c >= 2 && valid < 128) {
 #pragma unroll
               for (int i = 0; i < 32; ++i)
                 if (32 * c + i >= valid) cur[i] = __float_as_uint(-INFINITY);
@@ -572,7 +579,6 @@ __global__ void __launch_bounds__(FmhaPlan<D>::kThreads, 1)
               __syncwarp();
               if (lane == 0) mbar_arrive(p_full(t, static_cast<uint32_t>(c >> 1)));
             }
-            if (c < 3) tmem_wait_ld();
           }
         }
         const float2 a01 = __fadd2_rn(acc[0], acc[1]), a23 = __fadd2_rn(acc[2], acc[3]);
