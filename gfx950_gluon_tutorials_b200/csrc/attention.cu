@@ -135,6 +135,13 @@ __device__ __forceinline__ float2 poly_exp2x2(float2 x) {
                      __uint_as_float(__float_as_uint(q.y) + (__float_as_uint(t.y) << 23)));
 }
 
+// After tcgen05.wait::ld: ties these registers to this point, so that no use
+// of a value loaded asynchronously is scheduled before the wait (no code).
+__device__ __forceinline__ void regs_ready(uint32_t (&r)[32]) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(r[i]));
+}
+
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float m;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(m) : "f"(a), "f"(b), "f"(c));
@@ -545,9 +552,13 @@ __global__ void __launch_bounds__(FmhaPlan<D>::kThreads, 1)
           for (int c = 0; c < 4; ++c) {
             if (c == 2) {
               tmem_wait_ld();
+              regs_ready(buf[0]);
               tmem_ld_32x32b_x32(s_col + 96u, buf[1]);
             }
-            if (c == 3) tmem_wait_ld();
+            if (c == 3) {
+              tmem_wait_ld();
+              regs_ready(buf[1]);
+            }
             uint32_t cur[32];
 #pragma unroll
             for (int i = 0; i < 32; ++i) cur[i] = c < 2 ? s[32 * c + i] : buf[c - 2][i];
