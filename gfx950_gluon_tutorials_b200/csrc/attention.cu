@@ -48,9 +48,10 @@
 #define B2G_FMHA_POLY_PAIRS 0
 #endif
 
-// Suspend-time hint of the slow path of the bounded waits (0: plain probes).
+// Suspend-time hint of the slow path of the bounded waits (0: plain probes,
+// which hand over between the roles a little sooner).
 #ifndef B2G_FMHA_WAIT_HINT_NS
-#define B2G_FMHA_WAIT_HINT_NS 20000
+#define B2G_FMHA_WAIT_HINT_NS 0
 #endif
 
 namespace b2g {
