@@ -661,23 +661,42 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
         }
         if (!fok) break;
       }
+      // The chunks shared with the other accumulator go to registers first and
+      // are released at once, so the next tile's MMAs wait for three TMEM loads
+      // rather than for the conversion and stores of the chunks before them.
+      constexpr uint32_t kPre = kScaled ? SP::kOvlChunks : 0u;
+      uint32_t pre[kPre > 0 ? kPre : 1][32];
+      if constexpr (kPre > 0) {
+#pragma unroll
+        for (uint32_t k = 0; k < kPre; ++k)
+          tmem_ld_32x32b_x32(tbase + ((first_chunk + k) & 7u) * 32u, pre[k]);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if constexpr (CG == 1)
+            mbar_arrive(ovl_bar);
+          else
+            mbar_arrive_remote(map_to_cta(ovl_bar, 0));
+        }
+      }
 #pragma unroll 1
       for (uint32_t ci = 0; ci < 8; ++ci) {
         const uint32_t c = (first_chunk + ci) & 7u;
         uint32_t v[32];
-        tmem_ld_32x32b_x32(tbase + c * 32u, v);
-        tmem_wait_ld();
-        if constexpr (kScaled) {
-          if (ci == SP::kOvlChunks - 1) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-              if constexpr (CG == 1)
-                mbar_arrive(ovl_bar);
-              else
-                mbar_arrive_remote(map_to_cta(ovl_bar, 0));
+        bool have = false;
+        if constexpr (kPre > 0) {
+#pragma unroll
+          for (uint32_t k = 0; k < kPre; ++k)
+            if (ci == k) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] = pre[k][i];
+              have = true;
             }
-          }
+        }
+        if (!have) {
+          tmem_ld_32x32b_x32(tbase + c * 32u, v);
+          tmem_wait_ld();
         }
         if (w.role == kRoleContrib) {
           if (ring_fix) {
