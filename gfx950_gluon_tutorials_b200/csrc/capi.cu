@@ -38,7 +38,9 @@ struct Options {
   std::atomic<int64_t> pair{1};          // cta_group::2 CTA pairs
   std::atomic<int64_t> sk_mode{3};       // see make_plan
   std::atomic<int64_t> group_m{1};
-  std::atomic<int64_t> min_sk_iters{4};
+  // a split piece must span 16 stages: the fixed cost of publishing and adding
+  // a partial tile (~13 us at 4096 x 4096) must stay below the half tile it saves
+  std::atomic<int64_t> min_sk_iters{16};
   std::atomic<int64_t> timeout_ms{2000};
   std::atomic<int64_t> inject{0};
   std::atomic<int64_t> max_units{0};     // 0 = one unit per SM (pair)

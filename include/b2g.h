@@ -238,7 +238,8 @@ B2G_API int b2g_cast_e5m2(const void* src, int src_dtype, int64_t n, uint8_t* ds
                                  over the last full wave plus the partial one;
                                  3 (default): split each into equal k-chunks */
 #define B2G_OPT_GROUP_M 3     /* raster group height in tiles (default 1: row-major) */
-#define B2G_OPT_MIN_SK_ITERS 4 /* minimum k-iterations per stream-K unit (default 4) */
+#define B2G_OPT_MIN_SK_ITERS 4 /* minimum k-iterations (256-byte stages) per stream-K unit
+                                  or split piece (default 16) */
 #define B2G_OPT_TIMEOUT_MS 5  /* bounded-wait deadline in ms (default 2000) */
 #define B2G_OPT_INJECT_FLAG_TIMEOUT 6 /* test hook: stream-K owners wait for a flag
                                          value no contributor writes, so the wait
