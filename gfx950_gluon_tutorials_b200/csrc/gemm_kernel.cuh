@@ -15,9 +15,12 @@
 //   warps 2-5   epilogue: TMEM -> registers -> (split-tile fixup) -> bf16/fp16
 //               -> swizzled smem -> TMA store. Warp w reads TMEM lanes
 //               32*(w%4) .. 32*(w%4)+31.
-//   warp 6      (MXFP4) scale copier: one thread copies each stage's scale
-//               factors smem -> TMEM with tcgen05.cp into one of two TMEM
-//               slots, so the MMA thread's issue slots go to MMAs. For scaled
+//   warp 6      (MXFP4) scale copier: one thread copies each K chunk's scale
+//               factors smem -> TMEM with tcgen05.cp into one of four per-chunk
+//               TMEM slots, so the MMA thread's issue slots go to MMAs. A slot
+//               is refilled as soon as the MMAs of the chunk that used it
+//               complete, so the copies run up to three chunks ahead and their
+//               completion does not wait on the MMAs just issued. For scaled
 //               e5m2 (half the scale bytes per stage) the MMA thread issues
 //               the copies itself into a single slot, which measured faster.
 //
@@ -87,8 +90,8 @@ struct alignas(64) GemmParams {
 template <int KIND>
 struct KindTraits {
   static constexpr bool kScaled = KIND == kKindMXE5M2 || KIND == kKindMXFP4;
-  // scale factors copied by a dedicated warp into two TMEM slots (else by the
-  // MMA thread, in issue order with the MMAs, into one slot)
+  // scale factors copied by a dedicated warp into four per-chunk TMEM slots
+  // (else by the MMA thread, in issue order with the MMAs, into one slot)
   static constexpr bool kSfWarp = KIND == kKindMXFP4;
   // 4-scale groups (one 512-byte atom per 128 rows) per stage: a stage holds
   // 128 bytes of K per row = 128 e5m2 (4 scales) or 256 e2m1 (8 scales).
@@ -116,7 +119,11 @@ struct SmemPlan {
   static constexpr bool kScaled = KindTraits<KIND>::kScaled;
   static constexpr int kGps = KindTraits<KIND>::kGroupsPerStage;
   static constexpr bool kSfWarp = KindTraits<KIND>::kSfWarp;
-  static constexpr uint32_t kSfSlots = kSfWarp ? 2 : 1;
+  // The scale copier fills per-chunk slots (kSfSlots of them, so it can run
+  // up to three chunks ahead of the MMAs); the MMA thread's own copies use
+  // one slot of a whole stage.
+  static constexpr uint32_t kSfSlots = kSfWarp ? 4 : 1;
+  static constexpr int kSlotChunks = kSfWarp ? 1 : kKChunks;
   static constexpr uint32_t kThreads = kSfWarp ? 224 : 192;
   // per 128-byte K chunk
   static constexpr uint32_t kChunkA = 128 * 128;
@@ -139,8 +146,9 @@ struct SmemPlan {
   static constexpr uint32_t kSfbOff = kSfaOff + STAGES * kSfaBytes;
   static constexpr uint32_t kEpiOff = ((kSfbOff + STAGES * kSfbBytes) + 1023u) & ~1023u;
   static constexpr uint32_t kBarOff = kEpiOff + 4 * kEpiBufs * kEpiBufBytes;
-  // full[S], empty[S], acc_full[2], acc_empty[2], ovl, drain, fixup[4], scales[2]
-  static constexpr uint32_t kNumBars = 2 * STAGES + 12;
+  // full[S], empty[S], acc_full[2], acc_empty[2], ovl, drain, fixup[4],
+  // scales[4], scale slot free[4]
+  static constexpr uint32_t kNumBars = 2 * STAGES + 18;
   static constexpr uint32_t kMiscOff = kBarOff + kNumBars * 8;  // tmem slot, abort flag
   static constexpr uint32_t kBytes = kMiscOff + 16;
   // The carve-up starts on a 1024-byte boundary (128-byte-swizzled TMA tiles).
@@ -155,14 +163,14 @@ struct SmemPlan {
   // bytes the TMA lands per chunk on the leader's full barrier (both CTAs)
   static constexpr uint32_t kChunkTx = CG * (kChunkA + kChunkB + kChunkSfa + kChunkSfb);
 
-  // TMEM columns. Block-scaled kinds keep kSfSlots scale-factor slots (one
-  // stage each) at the top of the 512 columns: per chunk c and 4-scale group
-  // g, SFA takes 4 columns at (c * kGps + g) * 4 and SFB (256 rows) 8 columns
-  // after all SFA columns. The two accumulators then overlap by kOvlChunks
-  // 32-column chunks, which the epilogue drains first.
-  static constexpr uint32_t kSfaSlotCols = kScaled ? kKChunks * kGps * 4 : 0;
+  // TMEM columns. Block-scaled kinds keep kSfSlots scale-factor slots (of
+  // kSlotChunks chunks each) at the top of the 512 columns: per chunk c of a
+  // slot and 4-scale group g, SFA takes 4 columns at (c * kGps + g) * 4 and
+  // SFB (256 rows) 8 columns after all SFA columns. The two accumulators then
+  // overlap by kOvlChunks 32-column chunks, which the epilogue drains first.
+  static constexpr uint32_t kSfaSlotCols = kScaled ? kSlotChunks * kGps * 4 : 0;
   static constexpr uint32_t kSfSlotCols =
-      kScaled ? ((kSfSlots * (kKChunks * kGps * 12) + 31) / 32 * 32) / kSfSlots : 0;
+      kScaled ? ((kSfSlots * (kSlotChunks * kGps * 12) + 31) / 32 * 32) / kSfSlots : 0;
   static constexpr uint32_t kSfBase = 512 - kSfSlots * kSfSlotCols;
   static constexpr uint32_t kAccStride = kScaled ? kSfBase - 256 : 256;
   static constexpr uint32_t kOvlChunks = (256 - kAccStride) / 32;
@@ -329,6 +337,7 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
   const uint32_t drain_bar = bar0 + 8u * (2 * STAGES + 5);
   auto fix_bar = [&](uint32_t q) { return bar0 + 8u * (2 * STAGES + 6 + q); };
   auto sf_bar = [&](uint32_t slot) { return bar0 + 8u * (2 * STAGES + 10 + slot); };
+  auto sfree_bar = [&](uint32_t slot) { return bar0 + 8u * (2 * STAGES + 14 + slot); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SP::kMiscOff);
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + SP::kMiscOff + 4);
 
@@ -344,7 +353,10 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
     mbar_init(ovl_bar, 4 * CG);
     mbar_init(drain_bar, 1);
     for (uint32_t q = 0; q < 4; ++q) mbar_init(fix_bar(q), 1);
-    for (uint32_t slot = 0; slot < 2; ++slot) mbar_init(sf_bar(slot), 1);
+    for (uint32_t slot = 0; slot < 4; ++slot) {
+      mbar_init(sf_bar(slot), 1);
+      mbar_init(sfree_bar(slot), 1);
+    }
     *abort_flag = 0u;
     fence_mbarrier_init();
     prefetch_tensormap(&p.tmA);
@@ -459,7 +471,7 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
   } else if (warp == 1) {
     // ----------------------------------------------------------- MMA issue --
     if (leader && lane == 0) {
-      uint32_t it = 0, tcount = 0;
+      uint32_t it = 0, tcount = 0, q = 0;  // q counts K chunks (scale slots)
       WorkCursor cur = cursor_begin(p.plan, unit);
       WorkItem w;
       bool alive = true;
@@ -479,20 +491,23 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
             alive = false;
             break;
           }
-          const uint32_t slot = SP::kSfWarp ? (it & 1u) : 0u;
-          if constexpr (SP::kSfWarp) {
-            // this stage's scale factors, copied into `slot` by the scale copier
-            if (!wait_phase_fast<false>(sf_bar(slot), (it >> 1) & 1u, abort_flag, p,
-                                        B2G_SITE_SCALES)) {
-              alive = false;
-              break;
-            }
-          }
           tc_fence_after();
           const int32_t nc = min(kKChunks, p.k_chunks - k * kKChunks);
 #pragma unroll
           for (int32_t c = 0; c < kKChunks; ++c) {
           if (c >= nc) break;
+          // scale slot and chunk index inside it
+          [[maybe_unused]] const uint32_t slot = SP::kSfWarp ? (q & 3u) : 0u;
+          [[maybe_unused]] const int cs = SP::kSfWarp ? 0 : c;
+          if constexpr (SP::kSfWarp) {
+            // this chunk's scale factors, copied into `slot` by the scale copier
+            if (!wait_phase_fast<false>(sf_bar(slot), (q >> 2) & 1u, abort_flag, p,
+                                        B2G_SITE_SCALES)) {
+              alive = false;
+              break;
+            }
+            tc_fence_after();
+          }
           const uint32_t a_addr = sbase + SP::kAOff + s * SP::kABytes + c * SP::kChunkA;
           const uint32_t b_addr = sbase + SP::kBOff + s * SP::kBBytes + c * SP::kChunkB;
           const uint64_t adesc = sdesc_kmajor_sw128(a_addr);
@@ -524,15 +539,19 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
             } else {
               const int g = KIND == kKindMXFP4 ? static_cast<int>(j >> 1) : 0;
               const uint32_t sf_id = KIND == kKindMXFP4 ? ((j & 1u) * 2u) : j;
-              const uint32_t sfa_t = (tmem_base + SP::sfa_col(slot, c, g)) | (sf_id << 30);
-              const uint32_t sfb_t = (tmem_base + SP::sfb_col(slot, c, g)) | (sf_id << 30);
+              const uint32_t sfa_t = (tmem_base + SP::sfa_col(slot, cs, g)) | (sf_id << 30);
+              const uint32_t sfb_t = (tmem_base + SP::sfb_col(slot, cs, g)) | (sf_id << 30);
               if constexpr (KIND == kKindMXFP4)
                 mma_mxf4<CG>(d_tmem, ad, bd, make_idesc<KIND, CG>(sf_id), sfa_t, sfb_t, acc);
               else
                 mma_mxf8f6f4<CG>(d_tmem, ad, bd, make_idesc<KIND, CG>(sf_id), sfa_t, sfb_t, acc);
             }
           }
+          // the copier may refill this chunk's slot once these MMAs complete
+          if constexpr (SP::kSfWarp) tc_commit<CG>(sfree_bar(slot));
+          ++q;
           }
+          if (!alive) break;
           if constexpr (CG == 1)
             tc_commit<1>(empty_bar(s));
           else
@@ -554,55 +573,53 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
     // -------------------------------------------------------- scale copier --
     if constexpr (SP::kSfWarp) {
       if (leader && lane == 0) {
-        uint32_t it = 0;
+        uint32_t it = 0, q = 0;  // q counts K chunks, in the MMA thread's order
         WorkCursor cur = cursor_begin(p.plan, unit);
         WorkItem w;
         bool alive = true;
         while (alive && cursor_next(p.plan, unit, cur, w)) {
           for (int32_t k = w.k_begin; k < w.k_end; ++k, ++it) {
             const uint32_t s = it % STAGES, ph = (it / STAGES) & 1u;
-            const uint32_t slot = it & 1u;
             if (!wait_phase_fast<false>(full_bar(s), ph, abort_flag, p, B2G_SITE_FULL)) {
               alive = false;
               break;
             }
-            if (it >= 2) {
-              // the MMAs of two stages back read this slot: their completion
-              // is the ring's empty barrier for that stage
-              const uint32_t i2 = it - 2;
-              if (!wait_phase_fast<false>(empty_bar(i2 % STAGES), (i2 / STAGES) & 1u, abort_flag,
-                                          p, B2G_SITE_EMPTY)) {
-                alive = false;
-                break;
-              }
-            }
-            tc_fence_after();
             const int32_t nc = min(kKChunks, p.k_chunks - k * kKChunks);
 #pragma unroll
             for (int32_t c = 0; c < kKChunks; ++c) {
               if (c >= nc) break;
+              const uint32_t slot = q & 3u;
+              // the MMAs of the chunk four back read this slot
+              if (q >= 4 && !wait_phase_fast<false>(sfree_bar(slot), ((q >> 2) - 1u) & 1u,
+                                                    abort_flag, p, B2G_SITE_EMPTY)) {
+                alive = false;
+                break;
+              }
+              tc_fence_after();
               const uint32_t sfa_addr =
                   sbase + SP::kSfaOff + s * SP::kSfaBytes + c * SP::kChunkSfa;
               const uint32_t sfb_addr =
                   sbase + SP::kSfbOff + s * SP::kSfbBytes + c * SP::kChunkSfb;
 #pragma unroll
               for (int g = 0; g < kGps; ++g) {
-                tmem_cp_32x128b_x4<CG>(tmem_base + SP::sfa_col(slot, c, g),
+                tmem_cp_32x128b_x4<CG>(tmem_base + SP::sfa_col(slot, 0, g),
                                        sdesc_rows16(sfa_addr + g * 512));
 #pragma unroll
                 for (int rb = 0; rb < 2; ++rb)
-                  tmem_cp_32x128b_x4<CG>(tmem_base + SP::sfb_col(slot, c, g) + 4 * rb,
+                  tmem_cp_32x128b_x4<CG>(tmem_base + SP::sfb_col(slot, 0, g) + 4 * rb,
                                          sdesc_rows16(sfb_addr + (rb * kGps + g) * 512));
               }
+              tc_commit<CG>(sf_bar(slot));
+              ++q;
             }
-            tc_commit<CG>(sf_bar(slot));
+            if (!alive) break;
           }
         }
         // Drain: this thread's copies complete before TMEM can be freed.
-        if (it > 0) {
-          const uint32_t last = it - 1;
+        if (q > 0) {
+          const uint32_t last = q - 1;
           uint32_t spins = 0;
-          while (!mbar_try_wait(sf_bar(last & 1u), (last >> 1) & 1u) && spins < (1u << 22)) ++spins;
+          while (!mbar_try_wait(sf_bar(last & 3u), (last >> 2) & 1u) && spins < (1u << 22)) ++spins;
         }
       }
     }
