@@ -434,7 +434,11 @@ def time_attention(world: int, peaks: dict, peak_src: str, steps: int, warmup: i
             "roofline": {"bound": "tensor", "achieved": tf, "peak": peaks["bf16_tflops"],
                          "unit": "TFLOP/s", "frac": tf / peaks["bf16_tflops"],
                          "algorithmic_flops_per_launch": flops,
-                         "peak_source": f"{peak_src} bf16_tflops (burst)"},
+                         "peak_source": f"{peak_src} bf16_tflops (burst)",
+                         # the timed loop runs ~0.1 s under the power cap
+                         "peak_sustained": peaks.get("bf16_tflops_sustained"),
+                         "frac_of_sustained": (tf / peaks["bf16_tflops_sustained"]
+                                               if peaks.get("bf16_tflops_sustained") else None)},
             "launches_per_call": 1}
 
 
