@@ -19,8 +19,8 @@
 //               factors smem -> TMEM with tcgen05.cp into one of four per-chunk
 //               TMEM slots, so the MMA thread's issue slots go to MMAs. A slot
 //               is refilled as soon as the MMAs of the chunk that used it
-//               complete, so the copies run up to three chunks ahead and their
-//               completion does not wait on the MMAs just issued. For scaled
+//               complete (a commit per chunk), so the copier may run up to
+//               three chunks ahead of the MMA thread. For scaled
 //               e5m2 (half the scale bytes per stage) the MMA thread issues
 //               the copies itself into a single slot, which measured faster.
 //
