@@ -175,6 +175,68 @@ def max_over_ranks(x: float, world: int) -> float:
     return float(t.item())
 
 
+# ----------------------------------------------------------------- checker --
+# Parity of what was timed: after each leg's timed region, seeded 128 x 128
+# blocks of its output are recomputed on the CPU by the oracle (the
+# reference's dequantise-then-fp32-matmul, restated in oracle/ and pinned to
+# the reference's own functions) and compared under the build's tolerances.
+# The oracle is only the checker here; nothing it computes is timed.
+TOL = {"fp16": 1e-2, "bf16": 1e-2, "bf8": 3e-2, "mxfp4": 3e-2}
+
+
+def pick_blocks(M: int, N: int, n: int, seed: int, bm: int = 128, bn: int = 128) -> list:
+    """n seeded (row, col) origins of bm x bn blocks inside an M x N output."""
+    g = torch.Generator().manual_seed(seed)
+    out = []
+    for _ in range(n):
+        r0 = int(torch.randint(0, max(1, (M - bm) // 16 + 1), (1,), generator=g)) * 16
+        c0 = int(torch.randint(0, max(1, (N - bn) // 16 + 1), (1,), generator=g)) * 16
+        out.append((min(r0, max(0, M - bm)), min(c0, max(0, N - bn))))
+    return out
+
+
+def parity_gemm(kind: str, inp: dict, c: torch.Tensor, blocks: list, b_row0: int = 0) -> dict:
+    """Checks blocks of C = A B^T against the oracle. `inp` holds a, b (N x K
+    storage) and, for scaled kinds, sa / sb ((rows, K/32) E8M0 of any strides);
+    `b_row0` offsets B's rows (a block's columns c0.. use B rows b_row0 + c0..)."""
+    import numpy as np
+    from oracle import mx
+    worst, exact, n_el = 0.0, 0, 0
+    for r0, c0 in blocks:
+        rs, cs = slice(r0, r0 + 128), slice(b_row0 + c0, b_row0 + c0 + 128)
+        got = c[r0:r0 + 128, c0:c0 + 128].contiguous()
+        if kind in ("fp16", "bf16"):
+            a = inp["a"][rs].contiguous()
+            b = inp["b"][cs].contiguous()
+            if kind == "fp16":
+                ref = mx.gemm_f16_ref(a.cpu().numpy(), b.cpu().numpy()).astype(np.float32)
+                g32 = got.float().cpu().numpy()
+            else:
+                bits = lambda t: t.view(torch.int16).cpu().numpy().view(np.uint16)  # noqa: E731
+                ref_bits = mx.gemm_f16_ref(bits(a), bits(b), "bf16")
+                ref = mx.bf16_bits_to_f32(ref_bits)
+                g32 = got.float().cpu().numpy()
+                exact += int(np.sum(bits(got) == ref_bits))
+        else:
+            a = inp["a"][rs].contiguous().view(torch.uint8).cpu().numpy()
+            b = inp["b"][cs].contiguous().view(torch.uint8).cpu().numpy()
+            sa = inp["sa"][rs].cpu().numpy()
+            sb = inp["sb"][cs].cpu().numpy()
+            fn = mx.gemm_mxfp4_ref if kind == "mxfp4" else mx.gemm_mxe5m2_ref
+            ref_bits = fn(a, b, sa, sb)
+            got_bits = got.view(torch.int16).cpu().numpy().view(np.uint16)
+            ref = mx.bf16_bits_to_f32(ref_bits)
+            g32 = mx.bf16_bits_to_f32(got_bits)
+            exact += int(np.sum(got_bits == ref_bits))
+        n_el += got.numel()
+        worst = max(worst, mx.normalised_max_abs(g32, ref))
+    res = {"ok": bool(worst <= TOL[kind]), "max_norm_err": worst, "tol": TOL[kind],
+           "blocks": [list(b) for b in blocks], "checker": "oracle (CPU)"}
+    if kind != "fp16":
+        res["bit_exact_frac"] = exact / max(1, n_el)
+    return res
+
+
 # --------------------------------------------------------------- workloads --
 class Workload:
     """One GEMM configuration with rotating device inputs (cold L2 per step)."""
@@ -227,6 +289,15 @@ class Workload:
         if self.dtype_name == "bf8":
             return self.ops.gemm_f8(s["a"], s["b"], s["c"], a_scales=s["sa"], b_scales=s["sb"])
         return self.ops.gemm_mxf4(s["a"], s["b"], s["sa"], s["sb"], s["c"])
+
+    def check(self, seed: int, n_blocks: int = 2) -> dict:
+        """Parity of one more call on input set 0 (outside any timed region)."""
+        out = self.run(0)
+        torch.cuda.synchronize()
+        self.ops.check_status()
+        s = self.sets[0]
+        inp = {"a": s["a"], "b": s["b"], "sa": s.get("sa"), "sb": s.get("sb")}
+        return parity_gemm(self.dtype_name, inp, out, pick_blocks(self.M, self.N, n_blocks, seed))
 
     def input_bytes(self) -> int:
         s = self.sets[0]
@@ -378,8 +449,8 @@ def time_moe(world: int, peaks: dict, steps: int, warmup: int) -> dict:
     dev = torch.device("cuda", torch.cuda.current_device())
     gen = torch.Generator(device=dev).manual_seed(91)
     qa, sa = ops.quantize_mxfp4(torch.randn((E * rows, K), generator=gen, device=dev))
-    qb, sb = ops.quantize_mxfp4(torch.randn((E * N, K), generator=gen, device=dev))
-    sb = ops.block_scales(sb, K)
+    qb, sb_rows = ops.quantize_mxfp4(torch.randn((E * N, K), generator=gen, device=dev))
+    sb = ops.block_scales(sb_rows, K)
     offs = torch.arange(0, E * rows + 1, rows, dtype=torch.int32, device=dev)
     c = torch.empty((E * rows, N), dtype=torch.bfloat16, device=dev)
     for _ in range(warmup):
@@ -396,12 +467,26 @@ def time_moe(world: int, peaks: dict, steps: int, warmup: int) -> dict:
     ops.check_status()
     flops = 2.0 * E * rows * N * K
     tf = flops / (ms * 1e-3) / 1e12
+    # parity: a block of two experts' rows against the oracle with that
+    # expert's weights (expert e's B rows start at e * N)
+    sb_raw = sb_rows
+    checks = []
+    for e, (r0, c0) in zip((1, E - 2), pick_blocks(rows, N, 2, 911)):
+        seg = slice(e * rows, (e + 1) * rows)
+        inp = {"a": qa[seg], "b": qb, "sa": sa[seg], "sb": sb_raw}
+        checks.append(parity_gemm("mxfp4", inp, c[e * rows:(e + 1) * rows], [(r0, c0)],
+                                  b_row0=e * N))
+    parity = {"ok": all(x["ok"] for x in checks),
+              "max_norm_err": max(x["max_norm_err"] for x in checks), "tol": TOL["mxfp4"],
+              "bit_exact_frac": min(x["bit_exact_frac"] for x in checks),
+              "blocks": [[e, *x["blocks"][0]] for e, x in zip((1, E - 2), checks)],
+              "checker": "oracle (CPU), expert's own weight rows"}
     del qa, qb, sa, sb, c
     torch.cuda.empty_cache()
     return {"workload": f"{E} experts x {rows} tokens, N={N} K={K} MXFP4 per GPU",
             "ms_per_step": ms, "tflops_per_gpu": tf,
             "frac_of_measured": tf / tensor_peak("mxfp4", peaks),
-            "launches_per_step": 2}
+            "launches_per_step": 2, "parity": parity}
 
 
 def time_attention(world: int, peaks: dict, peak_src: str, steps: int, warmup: int) -> dict:
@@ -427,6 +512,22 @@ def time_attention(world: int, peaks: dict, peak_src: str, steps: int, warmup: i
     ops.check_status()
     flops = attention.compute_flops(B, H, S, S, D, False)
     tf = flops / (ms * 1e-3) / 1e12
+    # parity: 128 query rows of two heads against the float64 oracle under the
+    # reference's tolerance rule (kernels/attention/common.py:142-174)
+    from oracle import attention as oa
+    import numpy as np
+    checks = []
+    for h, (r0, _) in zip((3, H - 5), pick_blocks(S, 128, 2, 733)):
+        sl = slice(r0, r0 + 128)
+        ref = oa.sdpa_tiles(q[:, h:h + 1].float().cpu().numpy(),
+                            k[:, h:h + 1].float().cpu().numpy(),
+                            v[:, h:h + 1].float().cpu().numpy(), md.sm_scale, sl)
+        got = o[:, h:h + 1, sl].float().cpu().numpy()
+        ok, dmax, _ = oa.check_output(got, ref, "bfloat16")
+        checks.append((h, r0, ok, dmax, float(np.abs(ref).max())))
+    parity = {"ok": all(x[2] for x in checks), "max_abs_diff": max(x[3] for x in checks),
+              "rule": "reference _check_output: atol max(1e-3, 2 eps x max|ref|), rtol 1e-3",
+              "blocks": [[h, r0] for h, r0, *_ in checks], "checker": "oracle (CPU, float64)"}
     del q, k, v, o
     torch.cuda.empty_cache()
     return {"workload": f"FMHA forward B={B} HQ=HK={H} S={S} D={D} bf16 bhsd non-causal per GPU",
@@ -439,7 +540,7 @@ def time_attention(world: int, peaks: dict, peak_src: str, steps: int, warmup: i
                          "peak_sustained": peaks.get("bf16_tflops_sustained"),
                          "frac_of_sustained": (tf / peaks["bf16_tflops_sustained"]
                                                if peaks.get("bf16_tflops_sustained") else None)},
-            "launches_per_call": 1}
+            "launches_per_call": 1, "parity": parity}
 
 
 def time_allgather(w: Workload, world: int, iters: int = 10) -> dict | None:
@@ -501,16 +602,158 @@ def time_gemm_gather(w: Workload, world: int, iters: int, chunks: int = 4) -> di
     seq = timed(sequential)
     ovl = timed(overlapped)
     ops.check_status()
+    # parity of the peer copies: every slot of this rank's buffer equals the
+    # NCCL all-gather of the slabs each rank computed into its own slot
+    rank = torch.distributed.get_rank()
+    buf = overlapped()
+    torch.cuda.synchronize()
+    ref = gather_slabs(buf[rank].contiguous())
+    ok = torch.tensor([1 if torch.equal(ref, buf) else 0], device=buf.device)
+    torch.distributed.all_reduce(ok, op=torch.distributed.ReduceOp.MIN)
     return {"gemm_then_gather_ms": seq, "gemm_gather_p2p_overlapped_ms": ovl,
-            "overlap_chunks": chunks}
+            "overlap_chunks": chunks, "gather_parity_ok": bool(ok.item() == 1),
+            "gather_parity_check": "p2p-gathered [world][M][n] buffer equals the NCCL "
+                                   "all-gather of each rank's own slot (torch.equal)"}
+
+
+LARGE_M, LARGE_N, LARGE_K = 16384, 53248, 16384
+
+
+def _large_operands(dev, lo: int, hi: int, with_a: bool = True) -> dict:
+    """BASELINE configs[4] operands: A (16384 x 16384) and B rows [lo, hi) of
+    the 53248 x 16384 weight, N(0,1) quantised to MXFP4 by the config-3 rule.
+    B is drawn in 256-row blocks from generators seeded by block index, so a
+    shard is bit-identical to the same rows of the whole matrix at any GPU
+    count. Scales are stored as the reference stores them (M-contiguous)."""
+    from gfx950_gluon_tutorials_b200 import ops
+    K = LARGE_K
+    out = {}
+    if with_a:
+        g = torch.Generator(device=dev).manual_seed(4000)
+        x = torch.randn((LARGE_M, K), generator=g, device=dev)
+        out["a"], out["sa"] = ops.quantize_mxfp4(x, rows_pad=LARGE_M)
+        del x
+    x = torch.empty((hi - lo, K), device=dev)
+    for r in range(lo, hi, 256):
+        g = torch.Generator(device=dev).manual_seed(5000 + r // 256)
+        x[r - lo:min(hi, r + 256) - lo].normal_(generator=g)
+    out["b"], out["sb"] = ops.quantize_mxfp4(x, rows_pad=hi - lo)
+    del x
+    return out
+
+
+def _time_large_once(inp: dict, c: torch.Tensor, steps: int, warmup: int) -> float:
+    from gfx950_gluon_tutorials_b200 import a4w4, ops
+    for _ in range(warmup):
+        a4w4.matmul(inp["a"], inp["b"], inp["sa"], inp["sb"], c)
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        a4w4.matmul(inp["a"], inp["b"], inp["sa"], inp["sb"], c)
+    end.record()
+    torch.cuda.synchronize()
+    ops.check_status()
+    return start.elapsed_time(end) / steps
+
+
+def time_large(world: int, rank: int, peaks: dict, steps: int, warmup: int) -> dict:
+    """MXFP4 C = A B^T, M = 16384, N = 53248, K = 16384,
+    B split along N over the ranks (whole 256-column tiles), A replicated, no
+    collective in the timed loop. Reports the max-over-ranks time, the
+    aggregate rate, the single-GPU time of the whole problem measured in the
+    same run (rank 0 alone, after the sharded run), the resulting speed-up and
+    efficiency, per-rank parity of two seeded 128 x 128 blocks against the
+    oracle, and (N > 1) the separately timed NCCL all-gather of the C slabs."""
+    from gfx950_gluon_tutorials_b200.shard import gather_slabs, shard_range
+    dev = torch.device("cuda", torch.cuda.current_device())
+    M, N, K = LARGE_M, LARGE_N, LARGE_K
+    lo, hi = shard_range(N, world, rank, align=256)
+    inp = _large_operands(dev, lo, hi)
+    c = torch.empty((M, hi - lo), dtype=torch.bfloat16, device=dev)
+    barrier(world)
+    ms = max_over_ranks(_time_large_once(inp, c, steps, warmup), world)
+    parity = parity_gemm("mxfp4", inp, c, pick_blocks(M, hi - lo, 2, 6000 + rank))
+    flops = 2.0 * M * N * K
+    res = {"workload": "a4w4 MXFP4 16384x53248x16384, B split along N over the ranks, "
+                       "A replicated (BASELINE configs[4])",
+           "M": M, "N_total": N, "K": K, "N_per_gpu": hi - lo,
+           "steps": steps, "warmup": warmup, "ms": ms,
+           "tflops": flops / (ms * 1e-3) / 1e12,
+           "tflops_per_gpu": flops / world / (ms * 1e-3) / 1e12}
+    res["frac_of_measured"] = res["tflops_per_gpu"] / tensor_peak("mxfp4", peaks)
+    # every rank's parity, gathered
+    flag = torch.tensor([1.0 if parity["ok"] else 0.0, parity["max_norm_err"],
+                         parity["bit_exact_frac"]], dtype=torch.float64, device=dev)
+    if world > 1:
+        allp = [torch.empty_like(flag) for _ in range(world)]
+        torch.distributed.all_gather(allp, flag)
+    else:
+        allp = [flag]
+    allp = [p.tolist() for p in allp]
+    res["parity"] = {"ok": all(p[0] == 1.0 for p in allp), "tol": TOL["mxfp4"],
+                     "per_rank": [{"rank": r, "ok": p[0] == 1.0, "max_norm_err": p[1],
+                                   "bit_exact_frac": p[2]} for r, p in enumerate(allp)],
+                     "blocks_per_rank": 2, "checker": "oracle (CPU)"}
+    if world > 1:
+        # the separately timed NCCL all-gather of the C slabs, and a check that
+        # every gathered slot holds its owner's slab (checksums of checksums)
+        for _ in range(2):
+            out = gather_slabs(c)
+        barrier(world)
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        iters = 5
+        start.record()
+        for _ in range(iters):
+            out = gather_slabs(c)
+        end.record()
+        torch.cuda.synchronize()
+        gms = max_over_ranks(start.elapsed_time(end) / iters, world)
+        mine = c.view(torch.int16).to(torch.int64).sum().reshape(1)
+        sums = [torch.empty_like(mine) for _ in range(world)]
+        torch.distributed.all_gather(sums, mine)
+        slot = out.view(torch.int16).to(torch.int64).sum(dim=(1, 2))
+        ok = torch.equal(slot, torch.cat(sums))
+        okt = torch.tensor([1 if ok else 0], device=dev)
+        torch.distributed.all_reduce(okt, op=torch.distributed.ReduceOp.MIN)
+        total = out.numel() * out.element_size()
+        res["allgather"] = {"bytes": total, "ms": gms, "algbw_gbs": total / gms / 1e6,
+                            "busbw_gbs": total * (world - 1) / world / gms / 1e6,
+                            "parity_ok": bool(okt.item() == 1),
+                            "check": "per-slot int16 checksums equal the owners' checksums"}
+        del out
+    del inp, c
+    torch.cuda.empty_cache()
+    # single-GPU time of the whole problem, in the same run
+    if world == 1:
+        n1 = ms
+    else:
+        barrier(world)
+        n1 = 0.0
+        if rank == 0:
+            full = _large_operands(dev, 0, N)
+            cf = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+            n1 = _time_large_once(full, cf, steps, warmup)
+            del full, cf
+            torch.cuda.empty_cache()
+        n1 = max_over_ranks(n1, world)
+    res["single_gpu_ms"] = n1
+    res["single_gpu_tflops"] = flops / (n1 * 1e-3) / 1e12
+    res["speedup_vs_single_gpu"] = n1 / ms
+    res["efficiency"] = n1 / (world * ms)
+    return res
 
 
 def cpu_reference_tflops(M: int, N: int, K: int, budget_s: float, threads: int) -> dict:
-    """The reference's CPU path (oracle restatement: torch.matmul in fp16 on the
-    host cores, kernels/gemm/intra_wave/a16w16/bench.py:183) on a row sample of
-    the same workload, repeated until about `budget_s` seconds of work."""
+    """The reference's CPU path (torch.matmul in fp16 on the host cores,
+    kernels/gemm/intra_wave/a16w16/bench.py:183) on the whole BASELINE
+    configs[0] problem: one warm-up, then the median of three runs. Falls back
+    to a row sample when one run would take longer than `budget_s` / 4."""
     from oracle import reference_cpu
-    return reference_cpu.time_a16w16(M, N, K, budget_s=budget_s, threads=threads)
+    return reference_cpu.time_a16w16_full(M, N, K, threads=threads, runs=3,
+                                          max_run_s=budget_s / 4)
 
 
 def read_traffic(kernel_key: str):
@@ -532,61 +775,50 @@ def contract_main(args):
     peaks, peak_src = load_peaks()
     M, K = 4096, 8192
     n_local = 4096
-    if args.config == "large":
-        M, K = 16384, 16384
-        n_local = 53248 // world
-    results = {}
     clocks = ClockSampler(local)
-    head_name = "mxfp4" if args.config == "large" else args.dtype
+    head_name = args.dtype
     # enough rotating sets that one pass over them exceeds the 126 MB L2
     w = Workload("head", M, n_local, K, head_name, sets=1, seed=1234 + rank)
     per_set = w.set_bytes()
     nsets = max(2, min(8, int(640e6 // per_set) + 1))
-    if args.config == "large":
-        nsets = 2
     w = Workload("head", M, n_local, K, head_name, sets=nsets, seed=1234 + rank)
     clocks.start()
     marks: list = []
     ms = time_device(w, args.steps, args.warmup, world, marks)
     clock_info = clocks.stop((marks[0], marks[1]))
+    head_parity = w.check(seed=4242 + rank)
     flops_total = w.flops * world
     value = flops_total / (ms * 1e-3) / 1e12
     per_gpu = value / world
     peak = tensor_peak(head_name, peaks)
-    results["head"] = dict(ms=ms, tflops=value)
     by_dtype = {}
-    if args.config != "large" and not args.no_extra:
+    if not args.no_extra:
         # config 1's second case: 3840 x 3840 x 8192 fp16 (225 tiles)
-        wx = Workload("fp16_3840", 3840, 3840, 8192, "fp16", sets=4, seed=55 + rank)
-        msx = time_device(wx, args.steps, args.warmup, world)
-        tf = wx.flops * world / (msx * 1e-3) / 1e12
-        by_dtype["fp16_3840x3840x8192"] = {
-            "ms_per_step": msx, "tflops": tf, "tflops_per_gpu": tf / world,
-            "pct_of_nominal_dense_peak": 100.0 * tf / world / NOMINAL_DENSE_TFLOPS["fp16"],
-            "frac_of_measured": tf / world / tensor_peak("fp16", peaks),
-            "launches_per_step": wx.launches_per_step}
-        del wx
-        torch.cuda.empty_cache()
-        for dn in ("bf8", "mxfp4"):
-            wx = Workload(dn, M, n_local, K, dn, sets=4, seed=99 + rank)
+        cases = [("fp16_3840x3840x8192", 3840, 3840, 8192, "fp16", 55),
+                 ("bf8", M, n_local, K, "bf8", 99), ("mxfp4", M, n_local, K, "mxfp4", 99)]
+        for key, m_, n_, k_, dn, seed in cases:
+            wx = Workload(key, m_, n_, k_, dn, sets=4, seed=seed + rank)
             msx = time_device(wx, args.steps, args.warmup, world)
             tf = wx.flops * world / (msx * 1e-3) / 1e12
-            by_dtype[dn] = {
+            by_dtype[key] = {
                 "ms_per_step": msx, "tflops": tf, "tflops_per_gpu": tf / world,
                 "pct_of_nominal_dense_peak": 100.0 * tf / world / NOMINAL_DENSE_TFLOPS[dn],
                 "frac_of_measured": tf / world / tensor_peak(dn, peaks),
-                "launches_per_step": wx.launches_per_step}
+                "launches_per_step": wx.launches_per_step,
+                "parity": wx.check(seed=77 + len(key) + rank)}
             del wx
             torch.cuda.empty_cache()
     e2e_ms, h2d, d2h = time_e2e(w, max(3, args.steps // 5), min(args.warmup, 3), world)
     e2e_val = flops_total / (e2e_ms * 1e-3) / 1e12
     gather = time_allgather(w, world)
-    skinny = None if args.no_extra or args.config == "large" else time_skinny(world, peaks,
-                                                                               peak_src)
-    moe = None if args.no_extra or args.config == "large" else time_moe(
-        world, peaks, args.steps, args.warmup)
-    attn = None if args.no_extra or args.config == "large" else time_attention(
-        world, peaks, peak_src, args.steps, args.warmup)
+    del w
+    torch.cuda.empty_cache()
+    skinny = None if args.no_extra else time_skinny(world, peaks, peak_src)
+    moe = None if args.no_extra else time_moe(world, peaks, args.steps, args.warmup)
+    attn = None if args.no_extra else time_attention(world, peaks, peak_src, args.steps,
+                                                     args.warmup)
+    large = None if args.no_large else time_large(world, rank, peaks, args.large_steps,
+                                                  args.large_warmup)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_reference_tflops(M, n_local, K, args.cpu_budget, os.cpu_count() or 1)
@@ -603,14 +835,12 @@ def contract_main(args):
             "warmup": args.warmup,
             "ms_per_step": ms,
             "higher_is_better": True,
-            "scaling": "strong" if args.config == "large" else "weak",
+            "scaling": "weak",
             "vs_baseline": None,
             "dtype": head_name,
             "data": "synthetic (seeded N(0,1) inputs, BASELINE recipes)",
             "config": {
-                "workload": ("a4w4 MXFP4 16384x53248x16384, B split along N over the ranks "
-                             "(BASELINE configs[4])" if args.config == "large" else
-                             f"a16w16 {head_name} C=A*B^T M=4096 K=8192, 4096 columns of C per "
+                "workload": (f"a16w16 {head_name} C=A*B^T M=4096 K=8192, 4096 columns of C per "
                              "GPU, B sharded along N, A replicated (BASELINE configs[1])"),
                 "M": M, "N_per_gpu": n_local, "K": K, "N_total": n_local * world,
                 "parallelism": f"N-shard x{world}, no collective in the timed loop",
@@ -618,23 +848,27 @@ def contract_main(args):
             },
             "tflops_per_gpu": per_gpu,
             "pct_of_nominal_dense_peak": 100.0 * per_gpu / NOMINAL_DENSE_TFLOPS[head_name],
+            "parity": head_parity,
             "by_dtype": by_dtype,
             "roofline": {
                 "bound": "tensor", "achieved": per_gpu, "peak": peak, "unit": "TFLOP/s",
                 "frac": per_gpu / peak, "traffic": traffic,
+                "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one "
+                                   "cold-input launch (profiles/traffic.json)"
+                                   if traffic is not None else None),
                 "peak_source": (f"{peak_src} bf16_tflops (burst) x dtype ratio"
-                                if head_name != "fp16" else f"{peak_src} bf16_tflops (burst)"),
-                "algorithmic_flops_per_launch": w.flops,
-                "algorithmic_bytes_per_launch": w.input_bytes() + w.sets[0]["c"].numel() * 2,
+                                if head_name not in ("fp16", "bf16")
+                                else f"{peak_src} bf16_tflops (burst)"),
+                "algorithmic_flops_per_launch": w_flops(M, n_local, K),
+                "algorithmic_bytes_per_launch": algo_bytes(head_name, M, n_local, K),
             },
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_val, "unit": "TFLOPS", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
-                    "path": (f"public API ({'a4w4' if head_name == 'mxfp4' else 'a16w16'}.matmul) "
-                             "on pinned host buffers; each step uploads its inputs and downloads "
-                             "its C, overlapped with the neighbouring steps' GEMMs on separate "
-                             "streams")},
-            "gpu_launches": args.steps * w.launches_per_step,
+                    "path": ("public API (a16w16.matmul) on pinned host buffers; each step "
+                             "uploads its inputs and downloads its C, overlapped with the "
+                             "neighbouring steps' GEMMs on separate streams")},
+            "gpu_launches": args.steps * (1 if head_name in ("fp16", "bf16") else 2),
             "clocks": clock_info,
         }
         if gather is not None:
@@ -645,13 +879,28 @@ def contract_main(args):
             line["moe_grouped_mxfp4"] = moe
         if attn is not None:
             line["attention_fwd"] = attn
+        if large is not None:
+            line["large"] = large
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()
 
 
+def w_flops(M: int, N: int, K: int) -> float:
+    return 2.0 * M * N * K
+
+
+def algo_bytes(dtype_name: str, M: int, N: int, K: int) -> int:
+    """A + B (+ scales) + C bytes of one launch."""
+    eb = {"fp16": 2, "bf16": 2, "bf8": 1, "mxfp4": 0.5}[dtype_name]
+    scales = (M + N) * (K // 32) if dtype_name in ("bf8", "mxfp4") else 0
+    return int((M + N) * K * eb + scales + M * N * 2)
+
+
 def reference_main(args, rank, world):
-    """CPU reference arm: rank 0 times the reference path; other ranks exit."""
+    """CPU reference arm: rank 0 times the reference path; other ranks exit.
+    Each step is one whole BASELINE configs[0] problem (a row sample only if
+    one problem would take longer than --ref-step-s)."""
     if rank != 0:
         if world > 1:
             torch.distributed.destroy_process_group()
@@ -659,23 +908,21 @@ def reference_main(args, rank, world):
     M, K, n_local = 4096, 8192, 4096
     threads = os.cpu_count() or 1
     from oracle import reference_cpu
-    vals = []
-    info = None
-    for i in range(args.warmup + args.steps):
-        info = reference_cpu.time_a16w16(M, n_local, K, budget_s=args.ref_step_s,
-                                         threads=threads)
-        if i >= args.warmup:
-            vals.append(info["value"])
-    value = statistics.median(vals)
+    info = reference_cpu.time_a16w16_full(M, n_local, K, threads=threads,
+                                          runs=args.steps, warmup=args.warmup,
+                                          max_run_s=args.ref_step_s)
+    value = info["value"]
     line = {
         "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
-        "data": "synthetic (seeded N(0,1) inputs)", "impl": "reference",
-        "config": {"workload": "a16w16 fp16 C=A*B^T M=4096 N=4096 K=8192 (BASELINE configs[1]) "
+        "data": "synthetic (seeded N(0,1)/sqrt(K) inputs, BASELINE configs[0])",
+        "impl": "reference",
+        "config": {"workload": "a16w16 fp16 C=A*B^T M=4096 N=4096 K=8192 (BASELINE configs[0]/[1]) "
                                "on the host cores", "M": M, "N_per_gpu": n_local, "K": K},
-        "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": threads, "kind": "port",
-                         "sample": info["sample"]},
+        "ms_per_step": info["ms_per_run"],
+        "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": info["cores"],
+                         "kind": "port", "sample": info["sample"]},
         "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -685,10 +932,38 @@ def reference_main(args, rank, world):
 
 
 # ------------------------------------------------- reference bench surface --
+def surface_call(kernel: str, dn: str, M: int, N: int, K: int, seed: int):
+    """A fresh input set of the reference bench's recipe and the call on it,
+    C preallocated (the rotating copies of a, b and c)."""
+    from gfx950_gluon_tutorials_b200 import a4w4, a8w8, a16w16
+    g = torch.Generator(device="cuda").manual_seed(1000 + seed)
+    if kernel == "a16w16":
+        dt = torch.float16 if dn == "fp16" else torch.bfloat16
+        a = torch.randn((M, K), generator=g, device="cuda").to(dt)
+        b = torch.randn((N, K), generator=g, device="cuda").to(dt).T
+        c = torch.empty((M, N), device="cuda", dtype=dt)
+        return lambda: a16w16.matmul(a, b, c)
+    if kernel == "a8w8":
+        a = (torch.rand((M, K), generator=g, device="cuda").half() - 0.5).to(torch.float8_e5m2)
+        b = (torch.rand((N, K), generator=g, device="cuda").half().T - 0.5).to(torch.float8_e5m2)
+        return lambda: a8w8.matmul(a, b)
+    a = torch.randint(0, 256, (M, K // 2), generator=g, device="cuda", dtype=torch.uint8)
+    b = torch.randint(0, 256, (N, K // 2), generator=g, device="cuda", dtype=torch.uint8)
+    m_pad = (M + 255) // 256 * 256
+    sa = torch.randint(124, 128, (K // 32, m_pad), generator=g, device="cuda",
+                       dtype=torch.uint8).T[:M]
+    sb = torch.randint(124, 128, (K // 32, N), generator=g, device="cuda", dtype=torch.uint8).T
+    c = torch.empty((M, N), device="cuda", dtype=torch.bfloat16)
+    return lambda: a4w4.matmul(a, b, sa, sb, c)
+
+
 def reference_surface_main(args):
     """kernels/gemm/intra_wave/<kind>/bench.py: correctness then a TFLOPS table."""
     from gfx950_gluon_tutorials_b200 import a4w4, a8w8, a16w16, ops
     torch.cuda.set_device(0)
+    if args.version is not None:
+        print(f"[{args.kernel}] --version {args.version}: this build has one kernel per kind "
+              f"(gemm_kernel, tcgen05); running it", flush=True)
     ks = [args.K] if args.K else [512, 1024, 2048, 4096, 8192, 16384, 32768]
     M, N = args.M, args.N
     dtypes = args.dtype or (["fp16", "bf16"] if args.kernel == "a16w16" else ["-"])
@@ -731,9 +1006,21 @@ def reference_surface_main(args):
             print(f"[{args.kernel}] M={M} N={N} K={K} dtype={dn}: "
                   f"{'match' if ok else 'DIFFER'}", flush=True)
             if args.rocprof:
-                for _ in range(1000):
-                    fn()
+                # cold caches as kernels/gemm/intra_wave/a16w16/bench.py:190-241
+                # does it: enough copies of (a, b, c) to fill --rotating-buffer-size
+                # MB, launch i using copy i % copies
+                set_bytes = int((M + N) * K * elem) + M * N * 2
+                copies = max(1, args.rotating_buffer_size * 1024 * 1024 // set_bytes)
+                calls = [surface_call(args.kernel, dn, M, N, K, i) for i in range(copies)]
+                print(f"[{args.kernel}] M={M} N={N} K={K} dtype={dn}: rotating tensors: "
+                      f"{copies} copies, {copies * set_bytes / 1024 ** 2:.0f} MB", flush=True)
+                calls[0]()
                 torch.cuda.synchronize()
+                for i in range(1000):
+                    calls[i % copies]()
+                torch.cuda.synchronize()
+                ops.check_status()
+                del calls
                 print(f"[{args.kernel}] M={M} N={N} K={K}: 1000 iterations done", flush=True)
                 continue
             for _ in range(5):
@@ -759,16 +1046,25 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b2g", "reference"], default="b2g")
-    ap.add_argument("--config", choices=["default", "large"], default="default")
+    ap.add_argument("--config", choices=["default", "large"], default="default",
+                    help="large: only the headline and the BASELINE configs[4] object")
     ap.add_argument("--dtype", nargs="+", default=None)
-    ap.add_argument("--no-extra", action="store_true", help="skip the BF8/MXFP4 entries")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the 3840^2/BF8/MXFP4, small-M, MoE and attention entries")
+    ap.add_argument("--no-large", action="store_true",
+                    help="skip the BASELINE configs[4] (16384x53248x16384 MXFP4) object")
+    ap.add_argument("--large-steps", type=int, default=2,
+                    help="timed launches of configs[4] (about 7.5 s each on one GPU)")
+    ap.add_argument("--large-warmup", type=int, default=1)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--cpu-budget", type=float, default=8.0, help="seconds of CPU baseline work")
     ap.add_argument("--ref-step-s", type=float, default=4.0,
                     help="seconds of CPU work per --impl reference step")
     # reference bench surface
     ap.add_argument("--kernel", choices=["a16w16", "a8w8", "a4w4"], default=None)
-    ap.add_argument("--version", type=int, default=None, help="accepted for compatibility")
+    ap.add_argument("--version", type=int, default=None,
+                    help="the reference's tutorial version; this build has one kernel per "
+                         "kind, which every version runs (the surface says so)")
     ap.add_argument("--K", type=int, default=None)
     ap.add_argument("--M", type=int, default=4096)
     ap.add_argument("--N", type=int, default=4096)
@@ -784,6 +1080,9 @@ def main():
     if args.warmup < 3:
         log("note: raising --warmup to 3 (timing rule)")
         args.warmup = 3
+    if args.config == "large":
+        args.no_extra = True
+        args.no_large = False
     contract_main(args)
 
 

@@ -52,6 +52,7 @@ SIGNATURES = {
     "b2g_attention_fwd": (_c_int, [_vp, _vp, _vp, _vp, ctypes.POINTER(ctypes.c_int64), _c_int,
                                    _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
                                    ctypes.c_float, _vp, _vp, _vp]),
+    "b2g_selftest_poly_exp2": (_c_int, [_vp, _vp, _vp, _vp, _c_i64, _vp]),
     "b2g_gemm_mxf4_noalloc": (_c_int, [_vp, _c_i64, _vp, _c_i64, _vp, _c_i64, _c_i64, _vp,
                                        _c_i64, _c_i64, _vp, _c_i64, _c_int, _c_int, _c_int,
                                        _c_int, _vp, _vp]),

@@ -31,6 +31,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <cstdint>
@@ -100,10 +101,13 @@ struct FmhaPlan {
 // they do not all queue on the MUFU unit): x = i + f with i = round(x) and
 // f in [-0.5, 0.5]; 2^f from a cubic fitted here to minimise the relative error
 // on that interval (iteratively reweighted least squares; max relative error
-// 7.5e-5 in fp32, below half an fp16 ULP); 2^i added to the exponent field.
-// Inputs below -126 (masked keys are -inf) are clamped there: with 2^f in
-// [0.70, 1.42] the biased exponent 126 or 127 plus i >= -126 stays >= 0, so the
-// result is a tiny non-negative number, never a carry into the sign bit.
+// 7.5e-5 in fp32 for x in [-125.5, 8], below half an fp16 ULP); 2^i added to
+// the exponent field. Inputs below -126 (masked keys are -inf) are clamped
+// there: with 2^f in [0.70, 1.42] the biased exponent 126 or 127 plus
+// i >= -126 stays >= 0, so the result is a tiny non-negative number, never a
+// carry into the sign bit (at the clamp the exponent field reaches 0, so the
+// result is the subnormal 0.99986 * 2^-126 rather than 0.99993 * 2^-126).
+// b2g_selftest_poly_exp2 evaluates it on caller data for the tests.
 __device__ __forceinline__ float poly_exp2(float x) {
   constexpr float kRound = 12582912.0f;  // 1.5 * 2^23: adding it rounds to an integer
   x = fmaxf(x, -126.0f);
@@ -761,4 +765,41 @@ extern "C" int b2g_attention_fwd(const void* q, const void* k, const void* v, vo
                 : launch_fmha<128, false>(prm, batch, heads_q, seqlen_q, s);
   return bf16 ? launch_fmha<64, true>(prm, batch, heads_q, seqlen_q, s)
               : launch_fmha<64, false>(prm, batch, heads_q, seqlen_q, s);
+}
+
+// Evaluates the FMHA's FMA-pipe exponential on caller data: y_scalar[i] =
+// poly_exp2(x[i]), y_pair[i] = the paired form (elements 2j and 2j+1 of x go
+// through one poly_exp2x2), y_exp2f[i] = exp2f(x[i]) for comparison.
+__global__ void poly_exp2_probe_kernel(const float* __restrict__ x, float* __restrict__ y_scalar,
+                                       float* __restrict__ y_pair, float* __restrict__ y_exp2f,
+                                       int64_t n) {
+  const int64_t pairs = (n + 1) / 2;
+  for (int64_t j = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; j < pairs;
+       j += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t i0 = 2 * j, i1 = 2 * j + 1;
+    const float x0 = x[i0], x1 = i1 < n ? x[i1] : 0.0f;
+    const float2 e = b2g::poly_exp2x2(make_float2(x0, x1));
+    y_scalar[i0] = b2g::poly_exp2(x0);
+    y_pair[i0] = e.x;
+    y_exp2f[i0] = exp2f(x0);
+    if (i1 < n) {
+      y_scalar[i1] = b2g::poly_exp2(x1);
+      y_pair[i1] = e.y;
+      y_exp2f[i1] = exp2f(x1);
+    }
+  }
+}
+
+extern "C" int b2g_selftest_poly_exp2(const float* x, float* y_scalar, float* y_pair,
+                                      float* y_exp2f, int64_t n, void* stream) {
+  if (x == nullptr || y_scalar == nullptr || y_pair == nullptr || y_exp2f == nullptr)
+    return B2G_EINVAL;
+  if (n < 0) return B2G_ESHAPE;
+  if (n == 0) return B2G_OK;
+  const int64_t pairs = (n + 1) / 2;
+  const int blocks = static_cast<int>(std::min<int64_t>((pairs + 255) / 256, 148 * 8));
+  poly_exp2_probe_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, y_scalar, y_pair, y_exp2f, n);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? B2G_OK : static_cast<int>(e);
 }

@@ -442,16 +442,20 @@ int run_skinny(const GemmCall& c, int sms) {
   }
 }
 
-int run_gemm(const GemmCall& c) {
+// `fixed`: a geometry the caller already planned (and sized its scratch by);
+// null plans here from the current options.
+int run_gemm(const GemmCall& c, const Geometry* fixed = nullptr) {
   int rc = check_call(c);
   if (rc != B2G_OK) return rc;
   int dev = -1;
   cudaGetDevice(&dev);
   const int sms = current_sms();
   if (sms <= 0) return B2G_ENODEVICE;
-  if (c.groups == nullptr && use_skinny(c.kind, c.M)) return run_skinny(c, sms);
+  if (fixed == nullptr && c.groups == nullptr && use_skinny(c.kind, c.M)) return run_skinny(c, sms);
   const int b_rows = c.groups != nullptr ? c.n_groups * c.N : c.N;
-  const Geometry g = geometry(c.kind, c.M, c.N, c.K, sms, pair_capacity(dev, sms), b_rows);
+  const Geometry g = fixed != nullptr
+                         ? *fixed
+                         : geometry(c.kind, c.M, c.N, c.K, sms, pair_capacity(dev, sms), b_rows);
   if (g.total > 0 && (c.ws == nullptr || c.ws_bytes < g.total)) return B2G_EWORKSPACE;
   if (c.ws != nullptr && (reinterpret_cast<uintptr_t>(c.ws) & 255u) != 0) return B2G_EALIGN;
   uint8_t* ws = static_cast<uint8_t*>(c.ws);
@@ -546,6 +550,8 @@ int gemm_mxf4_fixed_scratch(const uint8_t* A, int64_t lda, const uint8_t* B, int
   cudaGetDevice(&dev);
   const int sms = current_sms();
   if (sms <= 0) return B2G_ENODEVICE;
+  // planned once: the capacity check, the flag clear and the launch all use
+  // this geometry, whatever b2g_set_option calls other threads make meanwhile
   const Geometry g = geometry(c.kind, c.M, c.N, c.K, sms, pair_capacity(dev, sms));
   if (g.total > capacity) return B2G_ECAPACITY;
   if (g.flags_bytes > 0) {
@@ -555,7 +561,7 @@ int gemm_mxf4_fixed_scratch(const uint8_t* A, int64_t lda, const uint8_t* B, int
         cudaMemsetAsync(static_cast<uint8_t*>(scratch) + g.flags_off, 0, g.flags_bytes, stream);
     if (e != cudaSuccess) return static_cast<int>(e);
   }
-  return run_gemm(c);
+  return run_gemm(c, &g);
 }
 
 

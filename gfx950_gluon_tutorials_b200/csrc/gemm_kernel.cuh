@@ -652,7 +652,6 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
       }();
       const bool ring_fix = last_item && w.role != kRoleFull && p.has_tmp != 0;
       uint8_t* ring = smem + quad * 32768u;
-      bool failed = false;
       int32_t glob_first = w.first_contrib, glob_n = w.n_contrib;
       if (w.role == kRoleOwner) {
         bool fok = true;
@@ -790,7 +789,6 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
         }
         ++nstore;
       }
-      if (failed) break;
       if (w.role == kRoleContrib) {
         if (ring_fix) {
           fence_proxy_async_smem();

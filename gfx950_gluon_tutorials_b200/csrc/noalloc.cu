@@ -10,14 +10,17 @@
 //    every call; cudaFree waits for the whole device, which a latency-bound
 //    loop cannot afford.
 //
-// The scratch is one file-scope __device__ array; every device the library's
-// module is loaded on has its own copy. Its address is looked up once per
-// device, by the first call made while that device is current, and is then
-// handed to the kernels like any workspace pointer. Nothing in this file, nor
-// in the path it calls, allocates device memory.
+// The scratch is one file-scope __device__ array; every CUDA context the
+// library's module is loaded in has its own copy. Its address belongs to that
+// context, so it is cached per device together with the unique ID of the
+// context it was looked up in (cuCtxGetId): a call made in another context on
+// the same device (after cudaDeviceReset, or a context a driver-API host made
+// current) looks the address up again in that context instead of using a
+// stale one. Nothing in this file, nor in the path it calls, allocates device
+// memory.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
-#include <atomic>
 #include <cstdint>
 #include <mutex>
 
@@ -29,26 +32,68 @@ static __device__ __align__(256) uint8_t g_noalloc_scratch[B2G_NOALLOC_SCRATCH_B
 namespace {
 
 constexpr int kMaxDevices = 64;
-std::atomic<void*> g_scratch_addr[kMaxDevices];
-std::mutex g_setup_mutex;
 
-// This device's copy of the scratch. The first call per device resolves it
-// (which may load this module onto the device); later calls read the cache.
+struct ScratchCache {
+  unsigned long long ctx_id;  // cuCtxGetId of the context `addr` belongs to
+  void* addr;                 // null: not looked up yet
+};
+ScratchCache g_cache[kMaxDevices];
+std::mutex g_cache_mutex;
+
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+
+// Unique ID of the context current on this thread (0 when none is current).
+int current_context_id(unsigned long long* id) {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(p);
+    cudaGetLastError();
+  });
+  if (get_current == nullptr || get_id == nullptr) return B2G_ENODEVICE;
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS) return B2G_ENODEVICE;
+  *id = 0;
+  if (ctx != nullptr && get_id(ctx, id) != CUDA_SUCCESS) return B2G_ENODEVICE;
+  return B2G_OK;
+}
+
+// The scratch of the context current on device `dev`. The first call in a
+// context resolves it with cudaGetSymbolAddress (which may load this module
+// into the context, and makes the device's primary context current if none
+// is); later calls in the same context read the cache.
 int scratch_for_device(int dev, void** out) {
   if (dev < 0 || dev >= kMaxDevices) return B2G_ENODEVICE;
-  void* p = g_scratch_addr[dev].load(std::memory_order_acquire);
-  if (p == nullptr) {
-    std::lock_guard<std::mutex> lock(g_setup_mutex);
-    p = g_scratch_addr[dev].load(std::memory_order_relaxed);
-    if (p == nullptr) {
-      const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-      if (e != cudaSuccess || p == nullptr) {
-        cudaGetLastError();  // do not leave the failure in the caller's error state
-        return e != cudaSuccess ? static_cast<int>(e) : B2G_ENODEVICE;
-      }
-      g_scratch_addr[dev].store(p, std::memory_order_release);
-    }
+  std::lock_guard<std::mutex> lock(g_cache_mutex);
+  unsigned long long id = 0;
+  int rc = current_context_id(&id);
+  if (rc != B2G_OK) return rc;
+  ScratchCache& c = g_cache[dev];
+  if (c.addr != nullptr && id != 0 && c.ctx_id == id) {
+    *out = c.addr;
+    return B2G_OK;
   }
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess || p == nullptr) {
+    cudaGetLastError();  // do not leave the failure in the caller's error state
+    return e != cudaSuccess ? static_cast<int>(e) : B2G_ENODEVICE;
+  }
+  // the lookup made a context current if none was: key the cache on it
+  rc = current_context_id(&id);
+  if (rc != B2G_OK || id == 0) return rc != B2G_OK ? rc : B2G_ENODEVICE;
+  c.ctx_id = id;
+  c.addr = p;
   *out = p;
   return B2G_OK;
 }

@@ -75,6 +75,9 @@ def check_status(device: torch.device | None = None, reset: bool = True) -> None
     st = status_tensor(device)
     code = int(st.item())
     if code != 0:
+        # GEMMs still running on other streams use their workspaces' flags and
+        # partial sums: let every stream of the device finish before clearing
+        torch.cuda.synchronize(device)
         with _ws_lock:
             for (idx, _), ws in _workspaces.items():
                 if idx == device.index:

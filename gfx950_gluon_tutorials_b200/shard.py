@@ -106,9 +106,11 @@ def gemm_gather_p2p(matmul: Callable[..., torch.Tensor], a: torch.Tensor,
         done.record(compute)
         copy.wait_event(done)
         with torch.cuda.stream(copy):
-            for p in range(world):
-                if p != rank:
-                    peers[p][rank, lo:hi].copy_(mine, non_blocking=True)
+            # rank r sends to r+1, r+2, ... in turn, so at any moment every GPU
+            # receives from one peer instead of all ranks writing to the same one
+            for j in range(1, world):
+                p = (rank + j) % world
+                peers[p][rank, lo:hi].copy_(mine, non_blocking=True)
     compute.wait_stream(copy)
     hdl.barrier()  # every rank's copies into this buffer have landed
     return buf

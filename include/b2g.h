@@ -144,11 +144,15 @@ B2G_API int b2g_gemm_mxf4(const uint8_t* A, int64_t lda, const uint8_t* B, int64
  *   array is zero when the library's module is loaded on a device, and each
  *   call also clears its flag words on `stream` (a memset, no allocation)
  *   before the launch; partial sums and relaid scales need no initial value.
- * - Set-up: the first call on each device, made while that device is
+ * - Set-up: the first call in each CUDA context, made while that context is
  *   current, looks up the scratch address (cudaGetSymbolAddress, which may
- *   load the module onto the device) together with the set-up every entry
- *   point does once per device. Make that first call before any stream
- *   capture begins.
+ *   load the module into the context) together with the set-up every entry
+ *   point does once per device. The address is cached per device with the
+ *   context's unique ID, so a call in another context (after
+ *   cudaDeviceReset, or in a context a driver-API host made current) looks
+ *   it up again rather than reuse an address of a destroyed context; the
+ *   array's contents do not survive a context's destruction. Make the first
+ *   call of each context before any stream capture begins.
  * - Races: one scratch per device means calls on the same device must not
  *   overlap on the GPU (use one stream, or order streams with events);
  *   overlapping calls corrupt each other's flags and partial sums. */
@@ -197,6 +201,15 @@ B2G_API int b2g_attention_fwd(const void* q, const void* k, const void* v, void*
                               const int64_t* strides, int batch, int heads_q, int heads_k,
                               int seqlen_q, int seqlen_k, int head_dim, int dtype,
                               float sm_scale, float* lse, int* status, void* stream);
+
+/* Diagnostic, no counterpart in the reference: evaluates the FMHA's FMA-pipe
+ * exponential (a cubic for 2^f, f in [-0.5, 0.5], plus an exponent-field add;
+ * relative error <= 7.5e-5 for x in [-125.5, 8], inputs below -126 clamped) on
+ * n device floats: y_scalar from the one-lane form, y_pair from the packed
+ * two-lane form the softmax uses (elements 2j, 2j+1 together), y_exp2f from
+ * CUDA's exp2f for comparison. Asynchronous on `stream`. */
+B2G_API int b2g_selftest_poly_exp2(const float* x, float* y_scalar, float* y_pair,
+                                   float* y_exp2f, int64_t n, void* stream);
 
 /* Blocked E8M0 scale layout: for each 128-row block and each group of 4
  * k-blocks (4 scales), 512 bytes in which byte r0*16 + r1*4 + j holds the

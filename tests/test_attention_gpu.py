@@ -176,3 +176,32 @@ def test_status_stays_clear_and_errors_raise(cuda_device):
     with pytest.raises(_lib.B2GError):
         attention.attention_fwd(q, q, q)  # head dim 96
     assert int(ops.status_tensor(q.device).item()) == 0
+
+
+def test_poly_exp2_relative_error_bound(cuda_device):
+    """The FMHA's FMA-pipe exponential (poly_exp2 and its packed two-lane form)
+    against float64 2^x and CUDA's exp2f: relative error <= 7.5e-5 on
+    [-125.5, 8]; inputs at or below the -126 clamp (masked keys are -inf) give
+    a tiny non-negative finite value; both forms agree bit for bit."""
+    dense = torch.linspace(-125.5, 8.0, 4_000_001, dtype=torch.float64).float()
+    steps = torch.arange(-125.5, 8.25, 0.25, dtype=torch.float64).float()   # f = 0, +-0.25, 0.5
+    nudged = torch.cat([steps.nextafter(torch.tensor(-1e9)), steps.nextafter(torch.tensor(1e9))])
+    x_in = torch.cat([dense, steps, nudged.clamp(-125.5, 8.0)]).cuda()
+    x_low = torch.tensor([-126.0, -126.5, -150.0, -1e30, float("-inf")], device="cuda")
+    x = torch.cat([x_in, x_low])
+    ys, yp, ye = (torch.empty_like(x) for _ in range(3))
+    rc = _lib.lib().b2g_selftest_poly_exp2(x.data_ptr(), ys.data_ptr(), yp.data_ptr(),
+                                           ye.data_ptr(), x.numel(),
+                                           torch.cuda.current_stream().cuda_stream)
+    assert rc == _lib.OK
+    torch.cuda.synchronize()
+    assert torch.equal(ys.view(torch.int32), yp.view(torch.int32)), "pair form differs"
+    n = x_in.numel()
+    exact = torch.exp2(x_in.double())
+    rel = ((ys[:n].double() - exact).abs() / exact).max().item()
+    rel_f = ((ys[:n].double() - ye[:n].double()).abs() / ye[:n].double()).max().item()
+    assert rel <= 7.5e-5, f"max relative error vs 2^x {rel:.3e}"
+    assert rel_f <= 7.6e-5, f"max relative error vs exp2f {rel_f:.3e}"
+    low = ys[n:]
+    assert bool(torch.isfinite(low).all()) and bool((low >= 0).all())
+    assert bool((low < 2.0 ** -125).all())

@@ -118,22 +118,139 @@ def test_a16w16_explicit_c_and_strided_rows(cuda_device):
     assert torch.isnan(c_store[:, N:]).all(), "wrote outside C"
 
 
-def test_a16w16_full_size_sampled_rows(cuda_device):
-    """Config-1 size (4096 x 4096 x 8192): the whole C against the oracle on a
-    seeded sample of 256 rows, and against the exact GPU product for all rows."""
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["fp16", "bf16"])
+def test_a16w16_full_size_sampled_rows(cuda_device, dtype):
+    """Config-1 size (4096 x 4096 x 8192), fp16 and bf16: the whole C against
+    the oracle on a seeded sample of 256 rows, and against the exact GPU
+    product for all rows."""
     M = N = 4096
     K = 8192
     g = torch.Generator(device="cuda").manual_seed(1)
-    a = (torch.randn((M, K), generator=g, device="cuda") / K ** 0.5).half()
-    b_t = (torch.randn((N, K), generator=g, device="cuda") / K ** 0.5).half()
+    a = (torch.randn((M, K), generator=g, device="cuda") / K ** 0.5).to(dtype)
+    b_t = (torch.randn((N, K), generator=g, device="cuda") / K ** 0.5).to(dtype)
     c = ops.gemm_f16(a, b_t)
     ops.check_status()
-    rows = torch.randperm(M, generator=torch.Generator().manual_seed(2))[:256]
-    ref = mx.gemm_f16_ref(a[rows.cuda()].cpu().numpy(), b_t.cpu().numpy()).astype(np.float32)
-    assert_close(as_f32(c[rows.cuda()]), ref, TOL_F16)
+    assert c.dtype == dtype
+    rows = torch.randperm(M, generator=torch.Generator().manual_seed(2))[:256].cuda()
+    if dtype == torch.float16:
+        ref = mx.gemm_f16_ref(a[rows].cpu().numpy(), b_t.cpu().numpy()).astype(np.float32)
+    else:
+        ref = mx.bf16_bits_to_f32(mx.gemm_f16_ref(bits16(a[rows]), bits16(b_t), "bf16"))
+    assert_close(as_f32(c[rows]), ref, TOL_F16, ref_atol=False)
     full = (a.float() @ b_t.float().T)
     err = ((c.float() - full).abs().max() / full.abs().max()).item()
     assert err <= TOL_F16
+
+
+def _gpu_normalised_err(c: torch.Tensor, ref: torch.Tensor) -> float:
+    return ((c.float() - ref).abs().max() / ref.abs().max()).item()
+
+
+def test_a8w8_scaled_cfg2_full_size(cuda_device):
+    """BASELINE config 2 at its benched size, 4096 x 4096 x 8192: N(0,1) data
+    quantised to e5m2 under E8M0 exponents U{-2..2} (bytes 125..129), bf16 out.
+    Sampled rows against the oracle (bit-identical bf16 expected, 3e-2
+    normalised bound asserted); all rows against the fp32 GPU product of the
+    dequantised operands."""
+    M = N = 4096
+    K = 8192
+    xa, xb, ea, eb = _mx_e5m2_inputs(M, N, K, seed=2002)
+    qa = ops.quantize_mxe5m2(xa, ea)
+    qb = ops.quantize_mxe5m2(xb, eb)
+    del xa, xb
+    ea_mc = ea.T.contiguous().T           # the reference's M-contiguous scale storage
+    c = a8w8.matmul_scaled(qa, qb.T, ea_mc, eb)
+    ops.check_status()
+    assert c.dtype == torch.bfloat16
+    rows = torch.randperm(M, generator=torch.Generator().manual_seed(2003))[:128].cuda()
+    ref = mx.gemm_mxe5m2_ref(qa[rows].view(torch.uint8).cpu().numpy(),
+                             qb.view(torch.uint8).cpu().numpy(),
+                             ea[rows].cpu().numpy(), eb.cpu().numpy())
+    got = bits16(c[rows])
+    assert_close(mx.bf16_bits_to_f32(got), mx.bf16_bits_to_f32(ref), TOL_F8, ref_atol=False)
+    print(f"cfg2 sampled rows bit-exact fraction {float(np.mean(got == ref)):.6f}")
+    da = qa.float() * torch.exp2(ea.float() - 127).repeat_interleave(32, dim=1)
+    db = qb.float() * torch.exp2(eb.float() - 127).repeat_interleave(32, dim=1)
+    full = da @ db.T
+    assert _gpu_normalised_err(c, full) <= TOL_F8
+
+
+def test_a8w8_unscaled_full_size(cuda_device):
+    """Unscaled e5m2 (the reference's a8w8 API, fp16 out) at 4096 x 4096 x 8192
+    on the reference's own recipe (rand - 0.5, cast to e5m2): its
+    allclose(atol=0.1) against the fp16-upcast torch product
+    (kernels/gemm/intra_wave/a8w8/bench.py:133-142) and the normalised bound
+    against the fp32 product; sampled rows against the oracle."""
+    M = N = 4096
+    K = 8192
+    g = torch.Generator(device="cuda").manual_seed(2004)
+    a = (torch.rand((M, K), generator=g, device="cuda").half() - 0.5).to(torch.float8_e5m2)
+    b = (torch.rand((N, K), generator=g, device="cuda").half().T - 0.5).to(torch.float8_e5m2)
+    c = a8w8.matmul(a, b)
+    ops.check_status()
+    assert c.dtype == torch.float16
+    full = a.float() @ b.float()
+    assert bool(torch.allclose(c.float(), full, atol=1e-1, rtol=0))
+    assert _gpu_normalised_err(c, full) <= TOL_F8
+    rows = torch.randperm(M, generator=torch.Generator().manual_seed(2005))[:128].cuda()
+    ref = mx.gemm_e5m2_ref(a[rows].view(torch.uint8).cpu().numpy(),
+                           b.T.contiguous().view(torch.uint8).cpu().numpy()).astype(np.float32)
+    assert_close(as_f32(c[rows]), ref, TOL_F8)
+
+
+def _decode_mxfp4_gpu(q: torch.Tensor, s: torch.Tensor) -> torch.Tensor:
+    """Dequantise packed e2m1 + E8M0 on the GPU through the reference's own
+    decode tables (kernels/gemm/intra_wave/a4w4/bench.py:80-112, committed as
+    tests/golden/decode_tables.npz)."""
+    t = golden("decode_tables.npz")
+    nib = torch.from_numpy(t["mxfp4"].reshape(256, 2)[:16, 0].copy()).cuda()
+    e8 = torch.from_numpy(t["e8m0"]).cuda()
+    codes = torch.stack([q & 0xF, q >> 4], dim=-1).reshape(q.shape[0], -1).long()
+    return nib[codes] * e8[s.long()].repeat_interleave(32, dim=1)
+
+
+@pytest.mark.parametrize("K", [512, 1024, 2048, 4096, 8192, 16384, 32768])
+@pytest.mark.parametrize("kind", ["fp16", "bf16", "bf8", "mxfp4"])
+def test_reference_correctness_sweep_m4096(cuda_device, kind, K):
+    """The reference benches' own correctness check (M = N = 4096, every K of
+    their sweep, kernels/gemm/intra_wave/{a16w16,a8w8,a4w4}/bench.py
+    test_correctness) on their input recipes: allclose(atol=0.1, rtol=0) and
+    the normalised bound against the fp32 GPU product of the same operands."""
+    M = N = 4096
+    g = torch.Generator(device="cuda").manual_seed(K + len(kind))
+    if kind in ("fp16", "bf16"):
+        dt = torch.float16 if kind == "fp16" else torch.bfloat16
+        a = torch.rand((M, K), generator=g, device="cuda").to(dt) - 0.5
+        b = torch.rand((N, K), generator=g, device="cuda").to(dt).T - 0.5
+        c = a16w16.matmul(a, b)
+        full, tol = a.float() @ b.float(), TOL_F16
+    elif kind == "bf8":
+        a = (torch.rand((M, K), generator=g, device="cuda").half() - 0.5).to(torch.float8_e5m2)
+        b = (torch.rand((N, K), generator=g, device="cuda").half().T - 0.5).to(torch.float8_e5m2)
+        c = a8w8.matmul(a, b)
+        full, tol = a.float() @ b.float(), TOL_F8
+    else:
+        a = torch.randint(0, 256, (M, K // 2), generator=g, device="cuda", dtype=torch.uint8)
+        b = torch.randint(0, 256, (N, K // 2), generator=g, device="cuda", dtype=torch.uint8)
+        sa = torch.randint(124, 128, (K // 32, M), generator=g, device="cuda",
+                           dtype=torch.uint8).T
+        sb = torch.randint(124, 128, (K // 32, N), generator=g, device="cuda",
+                           dtype=torch.uint8).T
+        c = a4w4.matmul(a, b, sa, sb)
+        full, tol = _decode_mxfp4_gpu(a, sa) @ _decode_mxfp4_gpu(b, sb).T, TOL_F8
+    ops.check_status()
+    if kind == "mxfp4":
+        # every product is a multiple of 2^-8 and every sum stays far inside
+        # fp32's 24 bits, so the fp32 product is exact: bf16 bits must agree
+        want = full.to(torch.bfloat16)
+        assert torch.equal(c.view(torch.int16), want.view(torch.int16)), \
+            f"{int((c != want).sum())} outputs differ from the exact sum rounded to bf16"
+    # the reference's allclose(atol=0.1); bf16 outputs above 32 are spaced
+    # wider than that, so bf16 also gets its rounding step (2^-8 relative)
+    rtol = 2.0 ** -8 if kind == "bf16" else 0.0
+    assert bool(torch.allclose(c.float(), full, atol=1e-1, rtol=rtol)), \
+        f"max abs diff {(c.float() - full).abs().max().item():.3e}"
+    assert _gpu_normalised_err(c, full) <= tol
 
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["fp16", "bf16"])

@@ -76,3 +76,62 @@ def test_cast_e5m2_matches_torch(cuda_device, dtype):
     np.testing.assert_array_equal(got, want)
     if dtype == torch.float32:
         np.testing.assert_array_equal(got, g["q"])
+
+
+def _check_nearest_e2m1(x: torch.Tensor, q: torch.Tensor, s: torch.Tensor) -> None:
+    """Every code the quantiser emitted, decoded through the reference's decode
+    tables (kernels/gemm/intra_wave/a4w4/bench.py:80-112, committed as
+    tests/golden/decode_tables.npz) and multiplied by its block's E8M0 scale,
+    is the grid value nearest to x / scale, with ties to the even code and
+    magnitudes above 6 saturated to 6. Scales follow the OCP MX rule
+    s = floor(log2(max|x|)) - 2 (byte s + 127, at least 0; an all-zero block
+    byte 0; a non-finite block byte 255 with zero codes)."""
+    t = golden("decode_tables.npz")
+    nib = torch.from_numpy(t["mxfp4"].reshape(256, 2)[:16, 0].copy()).cuda().double()
+    e8 = torch.from_numpy(t["e8m0"]).cuda().double()
+    mags = nib[:8]                                         # 0, .5, 1, 1.5, 2, 3, 4, 6
+    rows, K = x.shape
+    for r0 in range(0, rows, 256):
+        xb = x[r0:r0 + 256].double()
+        qb = q[r0:r0 + 256]
+        codes = torch.stack([qb & 0xF, qb >> 4], dim=-1).reshape(xb.shape[0], K).long()
+        sb = s[r0:r0 + 256].long()
+        blocks = xb.reshape(xb.shape[0], K // 32, 32)
+        finite = torch.isfinite(blocks).all(dim=2)
+        amax = blocks.abs().amax(dim=2)
+        # scale byte from the block max (finite blocks)
+        want_s = torch.where(amax > 0, torch.floor(torch.log2(amax)) - 2 + 127,
+                             torch.zeros_like(amax)).clamp(min=0)
+        want_s = torch.where(finite, want_s, torch.full_like(amax, 255))
+        assert torch.equal(sb, want_s.long()), "scale byte differs from the OCP MX rule"
+        assert bool((codes.reshape_as(blocks)[~finite] == 0).all()), "non-finite block codes"
+        scale = e8[sb].repeat_interleave(32, dim=1)
+        ok = finite.repeat_interleave(32, dim=1)
+        y = torch.where(ok, xb / torch.where(ok, scale, torch.ones_like(scale)),
+                        torch.zeros_like(xb))
+        dist = (y.abs().unsqueeze(-1) - mags).abs()            # (r, K, 8)
+        best = dist.min(dim=-1).values
+        got_mag = nib[codes & 7]
+        got_d = (y.abs() - got_mag).abs()
+        assert bool((got_d[ok] == best[ok]).all()), "a code is not the nearest grid value"
+        ties = (dist == best.unsqueeze(-1)).sum(dim=-1) > 1
+        assert bool(((codes & 1)[ok & ties] == 0).all()), "a tie did not round to the even code"
+        nz = ok & (got_mag > 0)
+        assert bool(((codes >> 3)[nz] == (y[nz] < 0).long()).all()), "sign bit"
+
+
+def test_quantize_mxfp4_nearest_grid_value_cfg3(cuda_device):
+    """BASELINE config-3 operands (4096 x 8192 N(0,1)) through the GPU quantiser,
+    pinned to the reference's decode table element by element."""
+    g = torch.Generator(device="cuda").manual_seed(3)
+    x = torch.randn((4096, 8192), generator=g, device="cuda")
+    q, s = ops.quantize_mxfp4(x, rows_pad=4096)
+    _check_nearest_e2m1(x, q, s)
+
+
+def test_quantize_mxfp4_nearest_grid_value_edges(cuda_device):
+    """The edge matrix (zero, negative-zero, NaN, inf, subnormal, near-FLT_MAX
+    and exact-tie blocks) pinned the same way."""
+    x = torch.from_numpy(_edge_matrix(1024, 4096, 99)).cuda()
+    q, s = ops.quantize_mxfp4(x)
+    _check_nearest_e2m1(x, q, s)
