@@ -90,9 +90,6 @@ struct alignas(64) GemmParams {
 template <int KIND>
 struct KindTraits {
   static constexpr bool kScaled = KIND == kKindMXE5M2 || KIND == kKindMXFP4;
-  // scale factors copied by a dedicated warp into four per-chunk TMEM slots
-  // (else by the MMA thread, in issue order with the MMAs, into one slot)
-  static constexpr bool kSfWarp = KIND == kKindMXFP4;
   // 4-scale groups (one 512-byte atom per 128 rows) per stage: a stage holds
   // 128 bytes of K per row = 128 e5m2 (4 scales) or 256 e2m1 (8 scales).
   static constexpr int kGroupsPerStage = KIND == kKindMXFP4 ? 2 : 1;
@@ -118,13 +115,12 @@ template <int KIND, int CG, int STAGES>
 struct SmemPlan {
   static constexpr bool kScaled = KindTraits<KIND>::kScaled;
   static constexpr int kGps = KindTraits<KIND>::kGroupsPerStage;
-  static constexpr bool kSfWarp = KindTraits<KIND>::kSfWarp;
-  // The scale copier fills per-chunk slots (kSfSlots of them, so it can run
-  // up to three chunks ahead of the MMAs); the MMA thread's own copies use
-  // one slot of a whole stage.
-  static constexpr uint32_t kSfSlots = kSfWarp ? 4 : 1;
-  static constexpr int kSlotChunks = kSfWarp ? 1 : kKChunks;
-  static constexpr uint32_t kThreads = kSfWarp ? 224 : 192;
+  // Block-scaled kinds: a scale-copy warp fills one TMEM scale slot per K
+  // chunk; the slots belong to stages in pairs (stage it uses slots
+  // 2 * (it % 2) + c), so a slot is free again once the MMAs of stage it - 2
+  // have completed, which the ring's empty barrier of that stage already says.
+  static constexpr uint32_t kSfSlots = kScaled ? 2 * kKChunks : 0;
+  static constexpr uint32_t kThreads = kScaled ? 224 : 192;
   // per 128-byte K chunk
   static constexpr uint32_t kChunkA = 128 * 128;
   static constexpr uint32_t kBRows = CG == 1 ? 256 : 128;
@@ -147,8 +143,8 @@ struct SmemPlan {
   static constexpr uint32_t kEpiOff = ((kSfbOff + STAGES * kSfbBytes) + 1023u) & ~1023u;
   static constexpr uint32_t kBarOff = kEpiOff + 4 * kEpiBufs * kEpiBufBytes;
   // full[S], empty[S], acc_full[2], acc_empty[2], ovl, drain, fixup[4],
-  // scales[4], scale slot free[4]
-  static constexpr uint32_t kNumBars = 2 * STAGES + 18;
+  // scale slots[4], copier drain + 3 spare, scales in smem[S]
+  static constexpr uint32_t kNumBars = 3 * STAGES + 18;
   static constexpr uint32_t kMiscOff = kBarOff + kNumBars * 8;  // tmem slot, abort flag
   static constexpr uint32_t kBytes = kMiscOff + 16;
   // The carve-up starts on a 1024-byte boundary (128-byte-swizzled TMA tiles).
@@ -160,26 +156,33 @@ struct SmemPlan {
       kBytes + 1024 <= kMaxDyn ? 1024u : (kBytes <= kMaxDyn ? (kMaxDyn - kBytes) & ~15u : 0u);
   static constexpr uint32_t kDynBytes = kBytes + kSlack;
 
-  // bytes the TMA lands per chunk on the leader's full barrier (both CTAs)
-  static constexpr uint32_t kChunkTx = CG * (kChunkA + kChunkB + kChunkSfa + kChunkSfb);
+  // bytes the TMA lands per chunk on the leader's full barrier (A and B of
+  // both CTAs) and on its scale barrier (both CTAs' scales)
+  static constexpr uint32_t kChunkTx = CG * (kChunkA + kChunkB);
+  static constexpr uint32_t kChunkTxSf = CG * (kChunkSfa + kChunkSfb);
 
-  // TMEM columns. Block-scaled kinds keep kSfSlots scale-factor slots (of
-  // kSlotChunks chunks each) at the top of the 512 columns: per chunk c of a
-  // slot and 4-scale group g, SFA takes 4 columns at (c * kGps + g) * 4 and
-  // SFB (256 rows) 8 columns after all SFA columns. The two accumulators then
-  // overlap by kOvlChunks 32-column chunks, which the epilogue drains first.
-  static constexpr uint32_t kSfaSlotCols = kScaled ? kSlotChunks * kGps * 4 : 0;
-  static constexpr uint32_t kSfSlotCols =
-      kScaled ? ((kSfSlots * (kSlotChunks * kGps * 12) + 31) / 32 * 32) / kSfSlots : 0;
-  static constexpr uint32_t kSfBase = 512 - kSfSlots * kSfSlotCols;
+  // TMEM columns. Block-scaled kinds keep kSfSlots scale-factor slots (one K
+  // chunk each) at the top of the 512 columns: per 4-scale group g, SFA (this
+  // CTA's 128 rows) takes 4 columns at g * 4 and SFB (256 rows) 8 columns at
+  // kSfaSlotCols + g * 8. SFA blocks sit on 4-column and SFB blocks on
+  // 8-column boundaries, as in every layout this kernel has run with. The two
+  // accumulators then overlap by kOvlChunks 32-column chunks, which the
+  // epilogue drains first.
+  static constexpr uint32_t kSfaSlotCols = kScaled ? (kGps * 4 + 7) / 8 * 8 : 0;
+  static constexpr uint32_t kSfSlotCols = kScaled ? kSfaSlotCols + kGps * 8 : 0;
+  static constexpr uint32_t kSfCols = (kSfSlots * kSfSlotCols + 31) / 32 * 32;
+  static constexpr uint32_t kSfBase = 512 - kSfCols;
   static constexpr uint32_t kAccStride = kScaled ? kSfBase - 256 : 256;
   static constexpr uint32_t kOvlChunks = (256 - kAccStride) / 32;
   static_assert(kAccStride % 32 == 0 && kOvlChunks < 8, "TMEM column plan");
-  __device__ static constexpr uint32_t sfa_col(uint32_t slot, int c, int g) {
-    return kSfBase + slot * kSfSlotCols + static_cast<uint32_t>(c * kGps + g) * 4;
+  static_assert(kSfBase % 8 == 0 && kSfSlotCols % 8 == 0 && kSfaSlotCols % 8 == 0,
+                "scale-factor blocks on 8-column boundaries");
+  static_assert(!kScaled || kKChunks == 2, "scale slots are paired with two-chunk stages");
+  __device__ static constexpr uint32_t sfa_col(uint32_t slot, int g) {
+    return kSfBase + slot * kSfSlotCols + static_cast<uint32_t>(g) * 4;
   }
-  __device__ static constexpr uint32_t sfb_col(uint32_t slot, int c, int g) {
-    return kSfBase + slot * kSfSlotCols + kSfaSlotCols + static_cast<uint32_t>(c * kGps + g) * 8;
+  __device__ static constexpr uint32_t sfb_col(uint32_t slot, int g) {
+    return kSfBase + slot * kSfSlotCols + kSfaSlotCols + static_cast<uint32_t>(g) * 8;
   }
 };
 
@@ -189,15 +192,20 @@ __device__ __forceinline__ void report_status(const GemmParams& p, int code) {
 
 // Bounded wait on an mbarrier phase. Returns false on timeout or when another
 // warp of the CTA has aborted.
-template <bool kClusterScope>
+// `kSleep`: each probe may suspend the thread for up to 20 us (woken when the
+// phase completes), for waits that normally last long; without it the probes
+// use the hardware's own short suspend, for hand-offs on the critical path.
+template <bool kClusterScope, bool kSleep = true>
 __device__ __noinline__ bool wait_phase(uint32_t bar, uint32_t parity, volatile uint32_t* abort_flag,
                                         const GemmParams& p, int site) {
-  // each probe may sleep up to 20 us; the deadline and the abort flag are
-  // checked between probes
+  // the deadline and the abort flag are checked between probes
   constexpr uint32_t kHintNs = 20000;
   auto probe = [&]() {
-    return kClusterScope ? mbar_try_wait_cluster_sleep(bar, parity, kHintNs)
-                         : mbar_try_wait_sleep(bar, parity, kHintNs);
+    if constexpr (kSleep)
+      return kClusterScope ? mbar_try_wait_cluster_sleep(bar, parity, kHintNs)
+                           : mbar_try_wait_sleep(bar, parity, kHintNs);
+    else
+      return kClusterScope ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity);
   };
   if (probe()) return true;
   const uint64_t t0 = globaltimer_ns();
@@ -223,6 +231,31 @@ __device__ __forceinline__ bool wait_phase_fast(uint32_t bar, uint32_t parity,
                                                 const GemmParams& p, int site) {
   if (mbar_try_wait(bar, parity)) return true;
   return wait_phase<kClusterScope>(bar, parity, abort_flag, p, site);
+}
+
+// Bounded wait that never suspends the thread, with CTA-scope probes: for the
+// MMA thread at a tile boundary. The epilogue warps of both CTAs arrive on
+// these barriers after their tcgen05.ld of the columns concerned has
+// completed (tcgen05.wait::ld) and a tcgen05.fence::before_thread_sync; the
+// MMA thread issues its next MMAs after tcgen05.fence::after_thread_sync. A
+// probe with cluster-scope acquire was measured at 0.5-1.2 us per success
+// while operand loads are in flight, a stall at every tile boundary.
+__device__ __noinline__ bool wait_spin(uint32_t bar, uint32_t parity, volatile uint32_t* abort_flag,
+                                       const GemmParams& p, int site) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+#pragma unroll 1
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i)
+      if (mbar_test_wait(bar, parity)) return true;
+    if (*abort_flag != 0u) return false;
+    if (globaltimer_ns() - t0 > p.timeout_ns) {
+      report_status(p, B2G_STATUS_TIMEOUT | site);
+      *abort_flag = 1u;
+      return false;
+    }
+  }
 }
 
 // Bounded wait for a global split-tile flag to reach `want`.
@@ -336,8 +369,13 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
   const uint32_t ovl_bar = bar0 + 8u * (2 * STAGES + 4);
   const uint32_t drain_bar = bar0 + 8u * (2 * STAGES + 5);
   auto fix_bar = [&](uint32_t q) { return bar0 + 8u * (2 * STAGES + 6 + q); };
+  // scale slot `slot` filled (the copier's copies issued and ordered before
+  // the MMA thread's next tcgen05 operations)
   auto sf_bar = [&](uint32_t slot) { return bar0 + 8u * (2 * STAGES + 10 + slot); };
-  auto sfree_bar = [&](uint32_t slot) { return bar0 + 8u * (2 * STAGES + 14 + slot); };
+  // the scale copier's own drain at exit
+  const uint32_t cdrain_bar = bar0 + 8u * (2 * STAGES + 14);
+  // stage s's scales landed in shared memory (loaded ahead of its A and B)
+  auto sffull_bar = [&](uint32_t s) { return bar0 + 8u * (2 * STAGES + 18 + s); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SP::kMiscOff);
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + SP::kMiscOff + 4);
 
@@ -345,6 +383,7 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
     for (uint32_t s = 0; s < STAGES; ++s) {
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), 1);
+      mbar_init(sffull_bar(s), 1);
     }
     for (uint32_t b = 0; b < 2; ++b) {
       mbar_init(accf_bar(b), 1);
@@ -353,10 +392,8 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
     mbar_init(ovl_bar, 4 * CG);
     mbar_init(drain_bar, 1);
     for (uint32_t q = 0; q < 4; ++q) mbar_init(fix_bar(q), 1);
-    for (uint32_t slot = 0; slot < 4; ++slot) {
-      mbar_init(sf_bar(slot), 1);
-      mbar_init(sfree_bar(slot), 1);
-    }
+    for (uint32_t slot = 0; slot < 4; ++slot) mbar_init(sf_bar(slot), 1);
+    mbar_init(cdrain_bar, 1);
     *abort_flag = 0u;
     fence_mbarrier_init();
     prefetch_tensormap(&p.tmA);
@@ -423,6 +460,34 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
           }
           // chunks past the end of K are neither loaded nor multiplied
           const int32_t nc = min(kKChunks, p.k_chunks - k * kKChunks);
+          if constexpr (kScaled) {
+            // the scale relayout launched just before this grid (programmatic
+            // dependency) must have finished before the first scale load
+            if (!sf_dep_done) {
+              grid_dependency_wait();
+              sf_dep_done = true;
+            }
+            // The stage's scales first, on their own barrier: they are small,
+            // land well before A and B, and the copier can move them into TMEM
+            // while the operands are still arriving.
+            if (leader)
+              mbar_arrive_expect_tx(sffull_bar(s), static_cast<uint32_t>(nc) * SP::kChunkTxSf);
+            const uint32_t sb_ = CG == 1 ? sffull_bar(s) : map_to_cta(sffull_bar(s), 0);
+            for (int32_t c = 0; c < nc; ++c) {
+              const int32_t kc = k * kKChunks + c;
+              // blocked scales: this CTA's 128-row group of A, both groups of the B tile
+              const uint32_t sfa_dst = sbase + SP::kSfaOff + s * SP::kSfaBytes + c * SP::kChunkSfa;
+              const uint32_t sfb_dst = sbase + SP::kSfbOff + s * SP::kSfbBytes + c * SP::kChunkSfb;
+              const int32_t sx = kc * kGps * 128;
+              if constexpr (CG == 1) {
+                tma_load_2d(sfa_dst, &p.tmSFA, sb_, sx, a_row >> 7);
+                tma_load_2d(sfb_dst, &p.tmSFB, sb_, sx, (b_base >> 7) + w.tn * 2);
+              } else {
+                tma_load_2d_pair(sfa_dst, &p.tmSFA, sb_, sx, a_row >> 7);
+                tma_load_2d_pair(sfb_dst, &p.tmSFB, sb_, sx, (b_base >> 7) + w.tn * 2);
+              }
+            }
+          }
           if (leader) mbar_arrive_expect_tx(full_bar(s), static_cast<uint32_t>(nc) * SP::kChunkTx);
           const uint32_t fb = CG == 1 ? full_bar(s) : map_to_cta(full_bar(s), 0);
           for (int32_t c = 0; c < nc; ++c) {
@@ -436,25 +501,6 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
               tma_load_2d_pair(a_dst, &p.tmA, fb, kc * 128, a_row);
               tma_load_2d_pair(b_dst, &p.tmB, fb, kc * 128, b_row);
             }
-            if constexpr (kScaled) {
-              // the scale relayout launched just before this grid (programmatic
-              // dependency) must have finished before the first scale load
-              if (!sf_dep_done) {
-                grid_dependency_wait();
-                sf_dep_done = true;
-              }
-              // blocked scales: this CTA's 128-row group of A, both groups of the B tile
-              const uint32_t sfa_dst = sbase + SP::kSfaOff + s * SP::kSfaBytes + c * SP::kChunkSfa;
-              const uint32_t sfb_dst = sbase + SP::kSfbOff + s * SP::kSfbBytes + c * SP::kChunkSfb;
-              const int32_t sx = kc * kGps * 128;
-              if constexpr (CG == 1) {
-                tma_load_2d(sfa_dst, &p.tmSFA, fb, sx, a_row >> 7);
-                tma_load_2d(sfb_dst, &p.tmSFB, fb, sx, (b_base >> 7) + w.tn * 2);
-              } else {
-                tma_load_2d_pair(sfa_dst, &p.tmSFA, fb, sx, a_row >> 7);
-                tma_load_2d_pair(sfb_dst, &p.tmSFB, fb, sx, (b_base >> 7) + w.tn * 2);
-              }
-            }
           }
         }
       }
@@ -465,22 +511,28 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
           const uint32_t s = i % STAGES, ph = (i / STAGES) & 1u;
           uint32_t spins = 0;
           while (!mbar_try_wait(full_bar(s), ph) && spins < (1u << 20)) ++spins;
+          if constexpr (kScaled) {
+            spins = 0;
+            while (!mbar_try_wait(sffull_bar(s), ph) && spins < (1u << 20)) ++spins;
+          }
         }
       }
     }
   } else if (warp == 1) {
     // ----------------------------------------------------------- MMA issue --
     if (leader && lane == 0) {
-      uint32_t it = 0, tcount = 0, q = 0;  // q counts K chunks (scale slots)
+      uint32_t it = 0, tcount = 0;
       WorkCursor cur = cursor_begin(p.plan, unit);
       WorkItem w;
       bool alive = true;
       while (alive && cursor_next(p.plan, unit, cur, w)) {
         const uint32_t b = tcount & 1u, aph = (tcount >> 1) & 1u;
-        if (!wait_phase<CG == 2>(acce_bar(b), aph ^ 1u, abort_flag, p, B2G_SITE_ACC_EMPTY)) break;
+        // tile boundary: the accumulator's previous tile drained (and, for the
+        // scaled kinds, the columns shared with the other accumulator read)
+        if (!wait_spin(acce_bar(b), aph ^ 1u, abort_flag, p, B2G_SITE_ACC_EMPTY)) break;
         if constexpr (kScaled) {
           if (tcount > 0 &&
-              !wait_phase<CG == 2>(ovl_bar, (tcount - 1) & 1u, abort_flag, p, B2G_SITE_OVERLAP))
+              !wait_spin(ovl_bar, (tcount - 1) & 1u, abort_flag, p, B2G_SITE_OVERLAP))
             break;
         }
         tc_fence_after();
@@ -496,12 +548,11 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
 #pragma unroll
           for (int32_t c = 0; c < kKChunks; ++c) {
           if (c >= nc) break;
-          // scale slot and chunk index inside it
-          [[maybe_unused]] const uint32_t slot = SP::kSfWarp ? (q & 3u) : 0u;
-          [[maybe_unused]] const int cs = SP::kSfWarp ? 0 : c;
-          if constexpr (SP::kSfWarp) {
+          [[maybe_unused]] const uint32_t slot = (it & 1u) * kKChunks + static_cast<uint32_t>(c);
+          if constexpr (kScaled) {
             // this chunk's scale factors, copied into `slot` by the scale copier
-            if (!wait_phase_fast<false>(sf_bar(slot), (q >> 2) & 1u, abort_flag, p,
+            // (its copies precede these MMAs in the tensor pipe)
+            if (!wait_phase_fast<false>(sf_bar(slot), (it >> 1) & 1u, abort_flag, p,
                                         B2G_SITE_SCALES)) {
               alive = false;
               break;
@@ -512,20 +563,6 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
           const uint32_t b_addr = sbase + SP::kBOff + s * SP::kBBytes + c * SP::kChunkB;
           const uint64_t adesc = sdesc_kmajor_sw128(a_addr);
           const uint64_t bdesc = sdesc_kmajor_sw128(b_addr);
-          if constexpr (kScaled && !SP::kSfWarp) {
-            // scale factors of this chunk: smem -> TMEM, in issue order with the MMAs
-            const uint32_t sfa_addr = sbase + SP::kSfaOff + s * SP::kSfaBytes + c * SP::kChunkSfa;
-            const uint32_t sfb_addr = sbase + SP::kSfbOff + s * SP::kSfbBytes + c * SP::kChunkSfb;
-#pragma unroll
-            for (int g = 0; g < kGps; ++g) {
-              tmem_cp_32x128b_x4<CG>(tmem_base + SP::sfa_col(0, c, g),
-                                     sdesc_rows16(sfa_addr + g * 512));
-#pragma unroll
-              for (int rb = 0; rb < 2; ++rb)
-                tmem_cp_32x128b_x4<CG>(tmem_base + SP::sfb_col(0, c, g) + 4 * rb,
-                                       sdesc_rows16(sfb_addr + (rb * kGps + g) * 512));
-            }
-          }
 #pragma unroll
           for (uint32_t j = 0; j < 4; ++j) {
             // +32 bytes of K per MMA inside the 128-byte swizzled row
@@ -539,19 +576,17 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
             } else {
               const int g = KIND == kKindMXFP4 ? static_cast<int>(j >> 1) : 0;
               const uint32_t sf_id = KIND == kKindMXFP4 ? ((j & 1u) * 2u) : j;
-              const uint32_t sfa_t = (tmem_base + SP::sfa_col(slot, cs, g)) | (sf_id << 30);
-              const uint32_t sfb_t = (tmem_base + SP::sfb_col(slot, cs, g)) | (sf_id << 30);
+              const uint32_t sfa_t = (tmem_base + SP::sfa_col(slot, g)) | (sf_id << 30);
+              const uint32_t sfb_t = (tmem_base + SP::sfb_col(slot, g)) | (sf_id << 30);
               if constexpr (KIND == kKindMXFP4)
                 mma_mxf4<CG>(d_tmem, ad, bd, make_idesc<KIND, CG>(sf_id), sfa_t, sfb_t, acc);
               else
                 mma_mxf8f6f4<CG>(d_tmem, ad, bd, make_idesc<KIND, CG>(sf_id), sfa_t, sfb_t, acc);
             }
           }
-          // the copier may refill this chunk's slot once these MMAs complete
-          if constexpr (SP::kSfWarp) tc_commit<CG>(sfree_bar(slot));
-          ++q;
           }
           if (!alive) break;
+          // frees the ring stage and, two stages later, this stage's scale slots
           if constexpr (CG == 1)
             tc_commit<1>(empty_bar(s));
           else
@@ -564,63 +599,71 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
           tc_commit_pair(accf_bar(b), 0x3);
         ++tcount;
       }
-      // Drain: all MMAs / copies issued by this thread complete before TMEM is freed.
+      // Drain: all MMAs issued by this thread complete before TMEM is freed.
       tc_commit<CG>(drain_bar);
       uint32_t spins = 0;
       while (!mbar_try_wait(drain_bar, 0) && spins < (1u << 22)) ++spins;
     }
   } else if (warp == 6) {
     // -------------------------------------------------------- scale copier --
-    if constexpr (SP::kSfWarp) {
+    if constexpr (kScaled) {
       if (leader && lane == 0) {
-        uint32_t it = 0, q = 0;  // q counts K chunks, in the MMA thread's order
+        uint32_t it = 0;
         WorkCursor cur = cursor_begin(p.plan, unit);
         WorkItem w;
         bool alive = true;
         while (alive && cursor_next(p.plan, unit, cur, w)) {
           for (int32_t k = w.k_begin; k < w.k_end; ++k, ++it) {
             const uint32_t s = it % STAGES, ph = (it / STAGES) & 1u;
-            if (!wait_phase_fast<false>(full_bar(s), ph, abort_flag, p, B2G_SITE_FULL)) {
+            // this stage's scales are in shared memory ...
+            if (!wait_phase_fast<false>(sffull_bar(s), ph, abort_flag, p, B2G_SITE_FULL)) {
               alive = false;
               break;
             }
-            const int32_t nc = min(kKChunks, p.k_chunks - k * kKChunks);
-#pragma unroll
-            for (int32_t c = 0; c < kKChunks; ++c) {
-              if (c >= nc) break;
-              const uint32_t slot = q & 3u;
-              // the MMAs of the chunk four back read this slot
-              if (q >= 4 && !wait_phase_fast<false>(sfree_bar(slot), ((q >> 2) - 1u) & 1u,
-                                                    abort_flag, p, B2G_SITE_EMPTY)) {
+            // ... and the MMAs of stage it - 2, the last readers of its slots, are done
+            if (it >= 2) {
+              const uint32_t pi = it - 2;
+              if (!wait_phase_fast<false>(empty_bar(pi % STAGES), (pi / STAGES) & 1u, abort_flag, p,
+                                          B2G_SITE_EMPTY)) {
                 alive = false;
                 break;
               }
-              tc_fence_after();
-              const uint32_t sfa_addr =
-                  sbase + SP::kSfaOff + s * SP::kSfaBytes + c * SP::kChunkSfa;
-              const uint32_t sfb_addr =
-                  sbase + SP::kSfbOff + s * SP::kSfbBytes + c * SP::kChunkSfb;
-#pragma unroll
-              for (int g = 0; g < kGps; ++g) {
-                tmem_cp_32x128b_x4<CG>(tmem_base + SP::sfa_col(slot, 0, g),
-                                       sdesc_rows16(sfa_addr + g * 512));
-#pragma unroll
-                for (int rb = 0; rb < 2; ++rb)
-                  tmem_cp_32x128b_x4<CG>(tmem_base + SP::sfb_col(slot, 0, g) + 4 * rb,
-                                         sdesc_rows16(sfb_addr + (rb * kGps + g) * 512));
-              }
-              tc_commit<CG>(sf_bar(slot));
-              ++q;
             }
-            if (!alive) break;
+            tc_fence_after();
+            const int32_t nc = min(kKChunks, p.k_chunks - k * kKChunks);
+#pragma unroll
+            for (int32_t c = 0; c < kKChunks; ++c) {
+              const uint32_t slot = (it & 1u) * kKChunks + static_cast<uint32_t>(c);
+              if (c < nc) {
+                const uint32_t sfa_addr =
+                    sbase + SP::kSfaOff + s * SP::kSfaBytes + c * SP::kChunkSfa;
+                const uint32_t sfb_addr =
+                    sbase + SP::kSfbOff + s * SP::kSfbBytes + c * SP::kChunkSfb;
+#pragma unroll
+                for (int g = 0; g < kGps; ++g) {
+                  tmem_cp_32x128b_x4<CG>(tmem_base + SP::sfa_col(slot, g),
+                                         sdesc_rows16(sfa_addr + g * 512));
+#pragma unroll
+                  for (int rb = 0; rb < 2; ++rb)
+                    tmem_cp_32x128b_x4<CG>(tmem_base + SP::sfb_col(slot, g) + 4 * rb,
+                                           sdesc_rows16(sfb_addr + (rb * kGps + g) * 512));
+                }
+              }
+              // Every slot of the stage is signalled (also a chunk past the end
+              // of K), so each slot's phase count stays it / 2. The fence orders
+              // the copies before the arrival: a tcgen05.cp followed by a
+              // tcgen05.mma that another thread issues after observing this
+              // arrival (and its own tcgen05.fence::after_thread_sync) runs in
+              // that order in the tensor pipe.
+              tc_fence_before();
+              mbar_arrive(sf_bar(slot));
+            }
           }
         }
         // Drain: this thread's copies complete before TMEM can be freed.
-        if (q > 0) {
-          const uint32_t last = q - 1;
-          uint32_t spins = 0;
-          while (!mbar_try_wait(sf_bar(last & 3u), (last >> 2) & 1u) && spins < (1u << 22)) ++spins;
-        }
+        tc_commit<CG>(cdrain_bar);
+        uint32_t spins = 0;
+        while (!mbar_try_wait(cdrain_bar, 0) && spins < (1u << 22)) ++spins;
       }
     }
   } else {
@@ -633,7 +676,7 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
     WorkItem w;
     while (cursor_next(p.plan, unit, cur, w)) {
       const uint32_t b = tcount & 1u, aph = (tcount >> 1) & 1u;
-      const bool ok = wait_phase<false>(accf_bar(b), aph, abort_flag, p, B2G_SITE_ACC_FULL);
+      const bool ok = wait_phase<false, false>(accf_bar(b), aph, abort_flag, p, B2G_SITE_ACC_FULL);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((quad * 32u) << 16) + b * SP::kAccStride;
@@ -693,7 +736,7 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
           if constexpr (CG == 1)
             mbar_arrive(ovl_bar);
           else
-            mbar_arrive_remote(map_to_cta(ovl_bar, 0));
+            mbar_arrive_remote_relaxed(map_to_cta(ovl_bar, 0));
         }
       }
 #pragma unroll 1
@@ -820,7 +863,7 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
         if constexpr (CG == 1)
           mbar_arrive(acce_bar(b));
         else
-          mbar_arrive_remote(map_to_cta(acce_bar(b), 0));
+          mbar_arrive_remote_relaxed(map_to_cta(acce_bar(b), 0));
       }
       ++tcount;
     }

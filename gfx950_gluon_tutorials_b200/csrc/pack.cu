@@ -304,20 +304,33 @@ __global__ void __launch_bounds__(256) sf_relayout_kernel(RelayoutArgs a, Relayo
     const IDX rb = qa / static_cast<IDX>(groups);
     const int32_t g = static_cast<int32_t>(qa - rb * static_cast<IDX>(groups));
     const int64_t row0 = static_cast<int64_t>(rb) * 128 + r0;
-    uint32_t v[4][4];
-#pragma unroll
-    for (int r1 = 0; r1 < 4; ++r1) {
-      const int64_t row = row0 + r1 * 32;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int32_t k = g * 4 + j;
-        v[r1][j] = (row < t.rows && k < kscales) ? __ldg(t.src + row * t.s0 + k * t.s1) : 127u;
-      }
-    }
     uint32_t w[4];
+    // K-contiguous scales with 4-byte aligned rows: one 32-bit load per row
+    // (the four scales of a group are adjacent); otherwise byte loads
+    const bool words = t.s1 == 1 && (t.s0 & 3) == 0 &&
+                       (reinterpret_cast<uintptr_t>(t.src) & 3u) == 0 && g * 4 + 3 < kscales;
+    if (words) {
 #pragma unroll
-    for (int r1 = 0; r1 < 4; ++r1)
-      w[r1] = v[r1][0] | (v[r1][1] << 8) | (v[r1][2] << 16) | (v[r1][3] << 24);
+      for (int r1 = 0; r1 < 4; ++r1) {
+        const int64_t row = row0 + r1 * 32;
+        w[r1] = row < t.rows ? __ldg(reinterpret_cast<const uint32_t*>(t.src + row * t.s0 + g * 4))
+                             : 0x7F7F7F7Fu;
+      }
+    } else {
+      uint32_t v[4][4];
+#pragma unroll
+      for (int r1 = 0; r1 < 4; ++r1) {
+        const int64_t row = row0 + r1 * 32;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int32_t k = g * 4 + j;
+          v[r1][j] = (row < t.rows && k < kscales) ? __ldg(t.src + row * t.s0 + k * t.s1) : 127u;
+        }
+      }
+#pragma unroll
+      for (int r1 = 0; r1 < 4; ++r1)
+        w[r1] = v[r1][0] | (v[r1][1] << 8) | (v[r1][2] << 16) | (v[r1][3] << 24);
+    }
     *reinterpret_cast<uint4*>(t.dst + (static_cast<int64_t>(rb) * groups + g) * 512 + r0 * 16) =
         make_uint4(w[0], w[1], w[2], w[3]);
   }
