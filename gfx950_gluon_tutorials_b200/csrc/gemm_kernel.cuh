@@ -178,6 +178,9 @@ struct SmemPlan {
   static_assert(kSfBase % 8 == 0 && kSfSlotCols % 8 == 0 && kSfaSlotCols % 8 == 0,
                 "scale-factor blocks on 8-column boundaries");
   static_assert(!kScaled || kKChunks == 2, "scale slots are paired with two-chunk stages");
+  // the epilogue's last tile uses the idle A/B ring: 128 KB of split-tile
+  // partials (4 warps x 32 KB) and 64 KB of output staging (4 warps x 16 KB)
+  static_assert(STAGES * (kABytes + kBBytes) >= 196608, "operand ring holds the last-tile staging");
   __device__ static constexpr uint32_t sfa_col(uint32_t slot, int g) {
     return kSfBase + slot * kSfSlotCols + static_cast<uint32_t>(g) * 4;
   }
@@ -730,6 +733,8 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
         for (uint32_t k = 0; k < kPre; ++k)
           tmem_ld_32x32b_x32(tbase + ((first_chunk + k) & 7u) * 32u, pre[k]);
         tmem_wait_ld();
+#pragma unroll
+        for (uint32_t k = 0; k < kPre; ++k) tmem_regs_ready(pre[k]);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
@@ -739,24 +744,13 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
             mbar_arrive_remote_relaxed(map_to_cta(ovl_bar, 0));
         }
       }
-#pragma unroll 1
-      for (uint32_t ci = 0; ci < 8; ++ci) {
+      // A unit's last tile stages all eight of its output chunks in the idle
+      // operand ring (beyond the 128 KB the split-tile partials may occupy),
+      // so its TMA stores go out back to back without waiting for one another.
+      uint8_t* const stage_last = smem + 131072u + quad * 16384u;
+      // One 32-column chunk: the split-tile part, then convert, stage and store.
+      auto body = [&](uint32_t ci, uint32_t (&v)[32]) {
         const uint32_t c = (first_chunk + ci) & 7u;
-        uint32_t v[32];
-        bool have = false;
-        if constexpr (kPre > 0) {
-#pragma unroll
-          for (uint32_t k = 0; k < kPre; ++k)
-            if (ci == k) {
-#pragma unroll
-              for (int i = 0; i < 32; ++i) v[i] = pre[k][i];
-              have = true;
-            }
-        }
-        if (!have) {
-          tmem_ld_32x32b_x32(tbase + c * 32u, v);
-          tmem_wait_ld();
-        }
         if (w.role == kRoleContrib) {
           if (ring_fix) {
             // 32 rows x 32 fp32 in the 128-byte swizzle, one box per chunk
@@ -774,7 +768,7 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
                      make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
                                  __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3])));
           }
-          continue;
+          return;
         }
         if (w.role == kRoleOwner) {
           if (ring_fix) {
@@ -807,13 +801,19 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
         // Convert and stage 32 rows x 32 columns in the 64-byte swizzle, then
         // one TMA store per warp (the tensor map clips rows / columns past C).
         // Chunks wholly outside C are skipped without touching the staging
-        // buffers, which alternate per store actually issued: the buffer being
-        // written is never the one the newest store may still be reading.
+        // buffers. Other tiles alternate two buffers per store actually
+        // issued: the buffer being written is never the one the newest store
+        // may still be reading.
         const int32_t x = n0 + static_cast<int32_t>(c * 32u);
-        if (x >= p.N || m0 >= p.M) continue;
-        uint8_t* buf = stage_base + (nstore & 1u) * SP::kEpiBufBytes;
-        if (lane == 0) bulk_wait_group_read<1>();
-        __syncwarp();
+        if (x >= p.N || m0 >= p.M) return;
+        uint8_t* buf;
+        if (last_item) {
+          buf = stage_last + c * SP::kEpiBufBytes;
+        } else {
+          buf = stage_base + (nstore & 1u) * SP::kEpiBufBytes;
+          if (lane == 0) bulk_wait_group_read<1>();
+          __syncwarp();
+        }
 #pragma unroll
         for (uint32_t pc = 0; pc < 4; ++pc) {
           uint4 q4;
@@ -831,6 +831,43 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
           bulk_commit_group();
         }
         ++nstore;
+      };
+      // Chunk ci's values in v: from the registers the overlap drain filled,
+      // or from the TMEM load issued one chunk earlier (fetch).
+      auto fetch = [&](uint32_t ci, uint32_t (&v)[32]) {
+        tmem_ld_32x32b_x32(tbase + ((first_chunk + ci) & 7u) * 32u, v);
+      };
+      auto in_pre = [](uint32_t ci) {
+        if constexpr (kPre == 0) return false;
+        else return ci < kPre;
+      };
+      auto take = [&](uint32_t ci, uint32_t (&v)[32]) {
+        if (in_pre(ci)) {
+          if constexpr (kPre > 0) {
+#pragma unroll
+            for (uint32_t k = 0; k < kPre; ++k)
+              if (ci == k) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = pre[k][i];
+              }
+          }
+        } else {
+          tmem_wait_ld();
+          tmem_regs_ready(v);
+        }
+      };
+      // Two register buffers: the next chunk's TMEM load is in flight while
+      // the current one is converted and stored.
+      uint32_t va[32], vb[32];
+      if constexpr (kPre == 0) fetch(0, va);
+#pragma unroll 1
+      for (uint32_t ci = 0; ci < 8; ci += 2) {
+        take(ci, va);
+        if (!in_pre(ci + 1)) fetch(ci + 1, vb);
+        body(ci, va);
+        take(ci + 1, vb);
+        if (ci + 2 < 8 && !in_pre(ci + 2)) fetch(ci + 2, va);
+        body(ci + 1, vb);
       }
       if (w.role == kRoleContrib) {
         if (ring_fix) {

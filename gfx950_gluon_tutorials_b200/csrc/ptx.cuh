@@ -491,6 +491,13 @@ __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// After tcgen05.wait::ld: ties the loaded registers to this point, so that
+// no use of an asynchronously loaded value is scheduled before the wait.
+__device__ __forceinline__ void tmem_regs_ready(uint32_t (&r)[32]) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(r[i]));
+}
+
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
