@@ -243,9 +243,11 @@ int encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t
   return r == CUDA_SUCCESS ? B2G_OK : B2G_ETENSORMAP;
 }
 
-// `after_relayout`: the scale relayout was launched just before on `stream`;
-// the GEMM may then start early (programmatic dependency) and waits for it
-// only before loading scales.
+// The GEMM is always launched with programmatic stream serialization, so its
+// launch overlaps the tail of the kernel before it. `after_relayout`: that
+// kernel is this library's scale relayout; the GEMM then waits for it only
+// before loading scales (pdl_mode 1), otherwise before any global access
+// (pdl_mode 2).
 template <int KIND, int CG, bool OB>
 int launch_gemm_t(const GemmParams& prm, int units, bool after_relayout, cudaStream_t stream) {
   constexpr bool kScaled = KindTraits<KIND>::kScaled;
@@ -277,14 +279,14 @@ int launch_gemm_t(const GemmParams& prm, int units, bool after_relayout, cudaStr
     attr[n_attr].val.clusterDim.z = 1;
     ++n_attr;
   }
-  if (after_relayout) {
-    attr[n_attr].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[n_attr].val.programmaticStreamSerializationAllowed = 1;
-    ++n_attr;
-  }
-  cfg.attrs = n_attr ? attr : nullptr;
+  attr[n_attr].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[n_attr].val.programmaticStreamSerializationAllowed = 1;
+  ++n_attr;
+  cfg.attrs = attr;
   cfg.numAttrs = n_attr;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, prm);
+  GemmParams prm2 = prm;
+  prm2.pdl_mode = after_relayout ? 1 : 2;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, prm2);
   return e == cudaSuccess ? B2G_OK : static_cast<int>(e);
 }
 

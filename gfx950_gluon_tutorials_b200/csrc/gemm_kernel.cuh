@@ -75,6 +75,12 @@ struct alignas(64) GemmParams {
   SkPlan plan;
   int32_t M, N, K;
   int32_t inject;       // test hook: 1 = split-tile owners wait for a flag nobody raises
+  // Launched with programmatic stream serialization. 1: right after this
+  // library's scale relayout, which itself waited for every earlier kernel,
+  // so A and B may be loaded at once and only the relaid scales wait;
+  // 2: after an arbitrary kernel, so every thread waits for it to complete
+  // before its first global memory access.
+  int32_t pdl_mode;
   int32_t prefetch;     // k-iterations the producer pulls into L2 ahead of its loads
   int32_t has_tmp;      // tmP is valid
   int32_t k_chunks;     // 128-byte K chunks per row (the last stage may hold fewer)
@@ -324,6 +330,10 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
   constexpr bool kScaled = SP::kScaled;
   constexpr int kGps = SP::kGps;
 
+  // The next kernel on the stream may be scheduled onto SMs as they free up
+  // (it waits for this grid to complete before touching memory).
+  if (threadIdx.x == 0) grid_launch_dependents();
+  if (p.pdl_mode == 2) grid_dependency_wait();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));

@@ -290,7 +290,11 @@ struct RelayoutArgs {
 template <typename IDX>
 __global__ void __launch_bounds__(256) sf_relayout_kernel(RelayoutArgs a, RelayoutArgs b,
                                                           int32_t kscales, int32_t groups) {
-  // the GEMM that reads this output may start its prologue and operand loads
+  // Launched with programmatic stream serialization: first wait for every
+  // earlier kernel (one may still be reading this workspace, or writing the
+  // scales or the GEMM's operands), then let the GEMM that reads this output
+  // start its prologue and its A/B loads.
+  grid_dependency_wait();
   grid_launch_dependents();
   const IDX n_a = static_cast<IDX>(a.row_blocks) * groups * 32;
   const IDX total = n_a + static_cast<IDX>(b.row_blocks) * groups * 32;
@@ -420,11 +424,19 @@ cudaError_t launch_sf_relayout(const uint8_t* sa, int64_t sa0, int64_t sa1, int 
   if (cudaGetDevice(&dev) == cudaSuccess)
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int grid = static_cast<int>(std::min<int64_t>(grid_for(work, 256), int64_t{sms} * 4));
-  if (work < (int64_t{1} << 31))
-    sf_relayout_kernel<uint32_t><<<grid, 256, 0, stream>>>(a, b, kscales, groups);
-  else
-    sf_relayout_kernel<int64_t><<<grid, 256, 0, stream>>>(a, b, kscales, groups);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = work < (int64_t{1} << 31)
+                            ? cudaLaunchKernelEx(&cfg, sf_relayout_kernel<uint32_t>, a, b, kscales, groups)
+                            : cudaLaunchKernelEx(&cfg, sf_relayout_kernel<int64_t>, a, b, kscales, groups);
+  return e;
 }
 
 }  // namespace b2g
