@@ -474,6 +474,11 @@ int run_gemm(const GemmCall& c, const Geometry* fixed = nullptr) {
                  static_cast<uint64_t>(c.ldb * eb), 128, g.cg == 1 ? 256 : 128,
                  CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc != B2G_OK) return rc;
+  // half-width tiles of the last partial wave load half as many B rows
+  rc = encode_2d(&prm.tmBh, CU_TENSOR_MAP_DATA_TYPE_UINT8, c.B, rb, static_cast<uint64_t>(b_rows),
+                 static_cast<uint64_t>(c.ldb * eb), 128, g.cg == 1 ? 128 : 64,
+                 CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc != B2G_OK) return rc;
   rc = encode_2d(&prm.tmC, CU_TENSOR_MAP_DATA_TYPE_UINT16, c.C, static_cast<uint64_t>(c.N),
                  static_cast<uint64_t>(c.M), static_cast<uint64_t>(c.ldc * 2), 32, 32,
                  CU_TENSOR_MAP_SWIZZLE_64B);
@@ -761,7 +766,7 @@ int b2g_set_option(int key, int64_t value) {
   switch (key) {
     case B2G_OPT_PAIR: g_opt.pair.store(value != 0); return B2G_OK;
     case B2G_OPT_SK_MODE:
-      if (value < 0 || value > 3) return B2G_EINVAL;
+      if (value < 0 || value > 4) return B2G_EINVAL;
       g_opt.sk_mode.store(value);
       return B2G_OK;
     case B2G_OPT_GROUP_M:
@@ -814,7 +819,7 @@ int64_t b2g_get_option(int key) {
 }
 
 int b2g_plan_query(int kind, int M, int N, int K, int num_sms, int32_t* out, int out_len) {
-  if (out == nullptr || out_len < 10) return B2G_EINVAL;
+  if (out == nullptr || out_len < 11) return B2G_EINVAL;
   if (kind < B2G_KIND_F16 || kind > B2G_KIND_MXFP4 || M < 1 || N < 1 || K < 1 || num_sms < 2)
     return B2G_EINVAL;
   const Geometry g = geometry(kind, M, N, K, num_sms);
@@ -828,6 +833,7 @@ int b2g_plan_query(int kind, int M, int N, int K, int num_sms, int32_t* out, int
   out[7] = g.launched;
   out[8] = g.plan.group_m;
   out[9] = g.plan.splits;
+  out[10] = g.plan.half;
   return B2G_OK;
 }
 
@@ -842,9 +848,10 @@ int b2g_plan_items(int kind, int M, int N, int K, int num_sms, int unit, int32_t
   int n = 0;
   while (cursor_next(g.plan, unit, cur, w)) {
     if (items != nullptr && n < max_items) {
-      int32_t* o = items + 9 * n;
+      int32_t* o = items + 10 * n;
       o[0] = w.tile; o[1] = w.tm; o[2] = w.tn; o[3] = w.k_begin; o[4] = w.k_end;
       o[5] = w.role; o[6] = w.first_contrib; o[7] = w.n_contrib; o[8] = w.contrib_stride;
+      o[9] = w.nh;
     }
     ++n;
   }

@@ -65,6 +65,7 @@ enum : int {
 struct alignas(64) GemmParams {
   CUtensorMap tmA;
   CUtensorMap tmB;
+  CUtensorMap tmBh;     // B with half-height boxes, for half-width (N = 128) tiles
   CUtensorMap tmC;
   CUtensorMap tmSFA;    // blocked scales of A (u32 view: 128 words per 128-row group)
   CUtensorMap tmSFB;    // blocked scales of B
@@ -102,6 +103,11 @@ struct KindTraits {
   // a/b format field of the instruction descriptor.
   static constexpr uint32_t kFmt = KIND == kKindF16 ? 0u : 1u;
 };
+
+// Instruction descriptor of a half-width (N = 128) tile: the N field halved.
+__device__ __forceinline__ uint32_t idesc_half(uint32_t idesc) {
+  return (idesc & ~(0x3Fu << 17)) | ((128u >> 3) << 17);
+}
 
 template <int KIND, int CG>
 __device__ __forceinline__ uint32_t make_idesc(uint32_t sf_id) {
@@ -165,6 +171,7 @@ struct SmemPlan {
   // bytes the TMA lands per chunk on the leader's full barrier (A and B of
   // both CTAs) and on its scale barrier (both CTAs' scales)
   static constexpr uint32_t kChunkTx = CG * (kChunkA + kChunkB);
+  static constexpr uint32_t kChunkTxHalf = CG * (kChunkA + kChunkB / 2);
   static constexpr uint32_t kChunkTxSf = CG * (kChunkSfa + kChunkSfb);
 
   // TMEM columns. Block-scaled kinds keep kSfSlots scale-factor slots (one K
@@ -411,6 +418,7 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
     fence_mbarrier_init();
     prefetch_tensormap(&p.tmA);
     prefetch_tensormap(&p.tmB);
+    prefetch_tensormap(&p.tmBh);
     prefetch_tensormap(&p.tmC);
     if (p.has_tmp) prefetch_tensormap(&p.tmP);
     if constexpr (kScaled) {
@@ -462,8 +470,17 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
         const int32_t a_row = w.tm * (128 * CG) + static_cast<int32_t>(rank) * 128;
         // grouped GEMM: the expert whose rows hold this M-tile picks B's rows
         const int32_t b_base = p.groups != nullptr ? expert_of(p, w.tm * (128 * CG)) * p.group_rows : 0;
-        const int32_t b_row =
-            b_base + w.tn * 256 + (CG == 2 ? static_cast<int32_t>(rank) * 128 : 0);
+        // a half-width tile (w.nh = 0 / 1) takes 128 of the tile's 256 B rows,
+        // 64 per CTA of a pair, through the half-height tensor map
+        const bool half = w.nh >= 0;
+        const int32_t b_rows_cta = (CG == 2 ? 128 : 256) >> (half ? 1 : 0);
+        const int32_t b_row = b_base + w.tn * 256 + (half ? w.nh * 128 : 0) +
+                              (CG == 2 ? static_cast<int32_t>(rank) * b_rows_cta : 0);
+        const CUtensorMap* tm_b = half ? &p.tmBh : &p.tmB;
+        const uint32_t chunk_tx = half ? SP::kChunkTxHalf : SP::kChunkTx;
+        // scales of B: the tile's first (or, for the second half, second)
+        // 128-row block comes first in the box
+        const int32_t sfb_row = (b_base >> 7) + w.tn * 2 + (half ? w.nh : 0);
         for (int32_t k = w.k_begin; k < w.k_end; ++k, ++it) {
           const uint32_t s = it % STAGES, ph = (it / STAGES) & 1u;
           if (p.prefetch > 0) prefetch_one();
@@ -494,14 +511,14 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
               const int32_t sx = kc * kGps * 128;
               if constexpr (CG == 1) {
                 tma_load_2d(sfa_dst, &p.tmSFA, sb_, sx, a_row >> 7);
-                tma_load_2d(sfb_dst, &p.tmSFB, sb_, sx, (b_base >> 7) + w.tn * 2);
+                tma_load_2d(sfb_dst, &p.tmSFB, sb_, sx, sfb_row);
               } else {
                 tma_load_2d_pair(sfa_dst, &p.tmSFA, sb_, sx, a_row >> 7);
-                tma_load_2d_pair(sfb_dst, &p.tmSFB, sb_, sx, (b_base >> 7) + w.tn * 2);
+                tma_load_2d_pair(sfb_dst, &p.tmSFB, sb_, sx, sfb_row);
               }
             }
           }
-          if (leader) mbar_arrive_expect_tx(full_bar(s), static_cast<uint32_t>(nc) * SP::kChunkTx);
+          if (leader) mbar_arrive_expect_tx(full_bar(s), static_cast<uint32_t>(nc) * chunk_tx);
           const uint32_t fb = CG == 1 ? full_bar(s) : map_to_cta(full_bar(s), 0);
           for (int32_t c = 0; c < nc; ++c) {
             const int32_t kc = k * kKChunks + c;
@@ -509,10 +526,10 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
             const uint32_t b_dst = sbase + SP::kBOff + s * SP::kBBytes + c * SP::kChunkB;
             if constexpr (CG == 1) {
               tma_load_2d(a_dst, &p.tmA, fb, kc * 128, a_row);
-              tma_load_2d(b_dst, &p.tmB, fb, kc * 128, b_row);
+              tma_load_2d(b_dst, tm_b, fb, kc * 128, b_row);
             } else {
               tma_load_2d_pair(a_dst, &p.tmA, fb, kc * 128, a_row);
-              tma_load_2d_pair(b_dst, &p.tmB, fb, kc * 128, b_row);
+              tma_load_2d_pair(b_dst, tm_b, fb, kc * 128, b_row);
             }
           }
         }
@@ -550,6 +567,7 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + b * SP::kAccStride;
+        const bool half = w.nh >= 0;  // N = 128 instructions on the first 64 B rows per CTA
         for (int32_t k = w.k_begin; k < w.k_end; ++k, ++it) {
           const uint32_t s = it % STAGES, ph = (it / STAGES) & 1u;
           if (!wait_phase_fast<false>(full_bar(s), ph, abort_flag, p, B2G_SITE_FULL)) {
@@ -583,18 +601,21 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
             const uint64_t bd = bdesc + 2u * j;
             const uint32_t acc = (k > w.k_begin || c > 0 || j > 0) ? 1u : 0u;
             if constexpr (KIND == kKindF16 || KIND == kKindBF16) {
-              mma_f16<CG>(d_tmem, ad, bd, make_idesc<KIND, CG>(0), acc);
+              const uint32_t id = make_idesc<KIND, CG>(0);
+              mma_f16<CG>(d_tmem, ad, bd, half ? idesc_half(id) : id, acc);
             } else if constexpr (KIND == kKindE5M2) {
-              mma_f8f6f4<CG>(d_tmem, ad, bd, make_idesc<KIND, CG>(0), acc);
+              const uint32_t id = make_idesc<KIND, CG>(0);
+              mma_f8f6f4<CG>(d_tmem, ad, bd, half ? idesc_half(id) : id, acc);
             } else {
               const int g = KIND == kKindMXFP4 ? static_cast<int>(j >> 1) : 0;
               const uint32_t sf_id = KIND == kKindMXFP4 ? ((j & 1u) * 2u) : j;
               const uint32_t sfa_t = (tmem_base + SP::sfa_col(slot, g)) | (sf_id << 30);
               const uint32_t sfb_t = (tmem_base + SP::sfb_col(slot, g)) | (sf_id << 30);
+              const uint32_t id = make_idesc<KIND, CG>(sf_id);
               if constexpr (KIND == kKindMXFP4)
-                mma_mxf4<CG>(d_tmem, ad, bd, make_idesc<KIND, CG>(sf_id), sfa_t, sfb_t, acc);
+                mma_mxf4<CG>(d_tmem, ad, bd, half ? idesc_half(id) : id, sfa_t, sfb_t, acc);
               else
-                mma_mxf8f6f4<CG>(d_tmem, ad, bd, make_idesc<KIND, CG>(sf_id), sfa_t, sfb_t, acc);
+                mma_mxf8f6f4<CG>(d_tmem, ad, bd, half ? idesc_half(id) : id, sfa_t, sfb_t, acc);
             }
           }
           }
@@ -694,7 +715,8 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((quad * 32u) << 16) + b * SP::kAccStride;
       const int32_t m0 = w.tm * (128 * CG) + static_cast<int32_t>(rank) * 128 + quad * 32;
-      const int32_t n0 = w.tn * 256;
+      const bool half = w.nh >= 0;  // a half-width tile fills chunks 0-3 only
+      const int32_t n0 = w.tn * 256 + (half ? w.nh * 128 : 0);
       // with overlapping accumulators the shared chunks are drained first
       const uint32_t first_chunk = kScaled ? (b == 0 ? 8u - SP::kOvlChunks : 0u) : 0u;
       // A split item that is this unit's last one finds the operand ring idle
@@ -761,6 +783,7 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
       // One 32-column chunk: the split-tile part, then convert, stage and store.
       auto body = [&](uint32_t ci, uint32_t (&v)[32]) {
         const uint32_t c = (first_chunk + ci) & 7u;
+        if (half && c >= 4u) return;
         if (w.role == kRoleContrib) {
           if (ring_fix) {
             // 32 rows x 32 fp32 in the 128-byte swizzle, one box per chunk

@@ -8,13 +8,18 @@
 // pair (cta_group::2); a unit walks its tiles in the same GROUP_M-swizzled
 // raster so concurrently running units share A and B panels in L2.
 //
-// Two ways to spread the tiles left after the full data-parallel waves:
+// Three ways to spread the tiles left after the full data-parallel waves:
 //   stream-K (modes 1, 2): their (tile, k) iteration space is cut into equal
 //     contiguous ranges, one per unit;
 //   split (mode 3): every leftover tile is cut into S equal k-chunks and chunk
 //     s of leftover tile j goes to unit s * leftover + j, so units running at
 //     the same time stream the same k-range of neighbouring tiles (their A and
-//     B panels stay shared in L2, which contiguous ranges lose).
+//     B panels stay shared in L2, which contiguous ranges lose);
+//   half (mode 4, when twice the leftover tiles fit on the units): every
+//     leftover tile runs as two independent half-width tiles (N = 128, whole
+//     K) on units 2j and 2j + 1. An N = 128 MMA takes half the time of an
+//     N = 256 one, so the last wave takes about half a tile and needs no
+//     partial-tile reduction; otherwise mode 4 falls back to mode 3.
 // Ownership rule (both): the unit that runs k-iteration 0 of a split tile
 // owns it. Every other unit touching the tile does so in the FIRST segment of
 // its range, writes an fp32 partial to its own workspace slot and raises a
@@ -44,6 +49,7 @@ struct SkPlan {
   int64_t sk_iters;          // (tiles - dp_tiles) * k_iters
   int32_t group_m;           // raster group height in tiles
   int32_t splits;            // split mode: k-chunks per leftover tile (0 = stream-K)
+  int32_t half;              // 1: leftover tiles run as half-width items (units [0, sk_units))
 };
 
 struct WorkItem {
@@ -54,6 +60,7 @@ struct WorkItem {
   int32_t role;      // kRoleFull / kRoleOwner / kRoleContrib
   // owner only: contributing units first, first + stride, ... (n_contrib of them)
   int32_t first_contrib, n_contrib, contrib_stride;
+  int32_t nh;        // -1: whole tile; 0 / 1: columns [0, 128) / [128, 256) of the tile
 };
 
 B2G_HD int32_t plan_tiles(const SkPlan& p) { return p.tiles_m * p.tiles_n; }
@@ -76,7 +83,8 @@ B2G_HD int64_t sk_range_begin(const SkPlan& p, int32_t u) {
 // Builds the plan. `sk_mode`: 0 = no splitting (all tiles data-parallel, the
 // last wave partial); 1 = stream-K over the partial last wave only;
 // 2 = stream-K over the last full wave plus the partial one; 3 = split the
-// tiles of the partial last wave into equal k-chunks.
+// tiles of the partial last wave into equal k-chunks; 4 = run them as
+// half-width tiles when they fit, else as mode 3.
 inline SkPlan make_plan(int32_t tiles_m, int32_t tiles_n, int32_t k_iters, int32_t units,
                         int32_t group_m, int32_t sk_mode, int32_t min_sk_iters) {
   SkPlan p{};
@@ -98,8 +106,14 @@ inline SkPlan make_plan(int32_t tiles_m, int32_t tiles_n, int32_t k_iters, int32
   p.sk_iters = static_cast<int64_t>(left) * k_iters;
   p.sk_units = 0;
   p.splits = 0;
+  p.half = 0;
   if (left == 0) return p;
-  if (sk_mode == 3) {
+  if (sk_mode == 4 && 2 * left <= units) {
+    p.half = 1;
+    p.sk_units = 2 * left;
+    return p;
+  }
+  if (sk_mode == 3 || sk_mode == 4) {
     // At most kMaxSplits pieces per leftover tile: the owner adds every
     // contributor's fp32 partial tile after its own k-range, and with more
     // than one contributor that serial reduction costs more than the shorter
@@ -132,7 +146,10 @@ struct WorkCursor {
 B2G_HD WorkCursor cursor_begin(const SkPlan& p, int32_t u) {
   WorkCursor c;
   c.dp_next = u;
-  if (u < p.sk_units) {
+  if (p.half && u < p.sk_units) {
+    c.sk_pos = 0;  // one half-width item
+    c.sk_end = 1;
+  } else if (u < p.sk_units) {
     c.sk_pos = sk_range_begin(p, u);
     c.sk_end = sk_range_begin(p, u + 1);
   } else {
@@ -146,6 +163,7 @@ B2G_HD bool cursor_next(const SkPlan& p, int32_t u, WorkCursor& c, WorkItem& w) 
   w.first_contrib = -1;
   w.n_contrib = 0;
   w.contrib_stride = 1;
+  w.nh = -1;
   if (c.dp_next < p.dp_tiles) {
     w.tile = c.dp_next;
     w.k_begin = 0;
@@ -156,6 +174,17 @@ B2G_HD bool cursor_next(const SkPlan& p, int32_t u, WorkCursor& c, WorkItem& w) 
     return true;
   }
   if (c.sk_pos >= c.sk_end) return false;
+  if (p.half) {
+    // half mode: units 2j, 2j + 1 take the two column halves of leftover tile j
+    w.tile = p.dp_tiles + (u >> 1);
+    w.nh = u & 1;
+    w.k_begin = 0;
+    w.k_end = p.k_iters;
+    w.role = kRoleFull;
+    c.sk_pos = c.sk_end;
+    tile_coords(p, w.tile, w.tm, w.tn);
+    return true;
+  }
   if (p.splits > 0) {
     // split mode: exactly one chunk per unit
     const int32_t left = p.sk_units / p.splits;

@@ -362,22 +362,23 @@ def cast_e5m2(x: torch.Tensor) -> torch.Tensor:
 
 def plan(kind: int, M: int, N: int, K: int, num_sms: int = 148) -> dict:
     """Host-side schedule summary (no GPU needed)."""
-    out = (ctypes.c_int32 * 10)()
-    check(lib().b2g_plan_query(kind, M, N, K, num_sms, out, 10), "b2g_plan_query")
+    out = (ctypes.c_int32 * 11)()
+    check(lib().b2g_plan_query(kind, M, N, K, num_sms, out, 11), "b2g_plan_query")
     keys = ("cta_group", "tiles_m", "tiles_n", "k_iters", "units", "dp_tiles", "sk_units",
-            "launched", "group_m", "splits")
+            "launched", "group_m", "splits", "half")
     return dict(zip(keys, list(out)))
 
 
 def plan_items(kind: int, M: int, N: int, K: int, unit: int, num_sms: int = 148) -> list[tuple]:
     """Work items (tile, tm, tn, k_begin, k_end, role, first_contrib, n_contrib,
-    contrib_stride) of one unit."""
+    contrib_stride, nh) of one unit; nh is -1 for a whole tile, 0 / 1 for the
+    first / second 128 columns of a half-width tile."""
     n = lib().b2g_plan_items(kind, M, N, K, num_sms, unit, None, 0)
     if n < 0:
         check(n, "b2g_plan_items")
-    buf = (ctypes.c_int32 * (9 * max(n, 1)))()
+    buf = (ctypes.c_int32 * (10 * max(n, 1)))()
     lib().b2g_plan_items(kind, M, N, K, num_sms, unit, buf, n)
-    return [tuple(buf[9 * i:9 * i + 9]) for i in range(n)]
+    return [tuple(buf[10 * i:10 * i + 10]) for i in range(n)]
 
 
 __all__ = [

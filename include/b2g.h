@@ -249,7 +249,10 @@ B2G_API int b2g_cast_e5m2(const void* src, int src_dtype, int64_t n, uint8_t* ds
                                  0: run as a partial wave; 1: stream-K (equal
                                  contiguous (tile, k) ranges per unit); 2: stream-K
                                  over the last full wave plus the partial one;
-                                 3 (default): split each into equal k-chunks */
+                                 3 (default): split each into equal k-chunks;
+                                 4: run each as two half-width (N = 128) tiles
+                                 when twice their count fits on the units, else
+                                 as 3 */
 #define B2G_OPT_GROUP_M 3     /* raster group height in tiles (default 1: row-major) */
 #define B2G_OPT_MIN_SK_ITERS 4 /* minimum k-iterations (256-byte stages) per stream-K unit
                                   or split piece (default 16) */
@@ -271,14 +274,15 @@ B2G_API int b2g_set_option(int key, int64_t value);
 B2G_API int64_t b2g_get_option(int key);
 
 /* Host-only view of the persistent schedule for a device with `num_sms` SMs
- * (no GPU needed). out[0..9] = {cta_group, tiles_m, tiles_n, k_iters, units,
- * dp_tiles, sk_units, launched_units, group_m, splits}. */
+ * (no GPU needed). out[0..10] = {cta_group, tiles_m, tiles_n, k_iters, units,
+ * dp_tiles, sk_units, launched_units, group_m, splits, half}; out_len >= 11. */
 B2G_API int b2g_plan_query(int kind, int M, int N, int K, int num_sms, int32_t* out, int out_len);
 
-/* Work items of one unit in execution order, 9 ints each: {tile, tm, tn,
+/* Work items of one unit in execution order, 10 ints each: {tile, tm, tn,
  * k_begin, k_end, role (0 full, 1 split-tile owner, 2 contributor),
- * first_contrib, n_contrib, contrib_stride}. Returns the item count (items may
- * be NULL). */
+ * first_contrib, n_contrib, contrib_stride, nh (-1 whole tile, 0 / 1 first /
+ * second 128 columns of a half-width tile)}. Returns the item count (items
+ * may be NULL). */
 B2G_API int b2g_plan_items(int kind, int M, int N, int K, int num_sms, int unit, int32_t* items,
                    int max_items);
 

@@ -51,6 +51,9 @@ def assert_close(c: np.ndarray, ref: np.ndarray, tol: float, ref_atol: bool = Tr
     dict(pair=1, sk=1, min_sk=1, units=5),   # few units: deep stream-K splits
     dict(pair=0, sk=2, min_sk=1, units=7),
     dict(pair=1, sk=3, min_sk=1, units=9),
+    dict(pair=1, sk=4, min_sk=4, units=0),   # leftover tiles as half-width tiles
+    dict(pair=0, sk=4, min_sk=4, units=0),
+    dict(pair=1, sk=4, min_sk=1, units=13),  # few units: halves fit only sometimes
 ], ids=lambda d: f"pair{d['pair']}-sk{d['sk']}-min{d['min_sk']}-u{d['units']}")
 def sched(request, cuda_device):
     """Main-kernel schedule variants; the small-M swap-AB kernel is switched off

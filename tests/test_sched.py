@@ -26,7 +26,7 @@ SHAPES = [
 ]
 
 
-@pytest.fixture(params=[(0, 1), (1, 1), (2, 1), (3, 1), (1, 0), (2, 0), (3, 0)],
+@pytest.fixture(params=[(0, 1), (1, 1), (2, 1), (3, 1), (4, 1), (1, 0), (2, 0), (3, 0), (4, 0)],
                 ids=lambda p: f"sk{p[0]}-pair{p[1]}")
 def options(request):
     sk, pair = request.param
@@ -53,12 +53,18 @@ def test_schedule_covers_every_iteration_once(options, shape, num_sms):
     for u in range(p["launched"]):
         items = ops.plan_items(kind, M, N, K, u, num_sms)
         seen_sk = False
-        for idx, (t, tm, tn, kb, ke, role, first, n_c, stride) in enumerate(items):
+        for idx, (t, tm, tn, kb, ke, role, first, n_c, stride, nh) in enumerate(items):
             assert 0 <= t < tiles and 0 <= tm < p["tiles_m"] and 0 <= tn < p["tiles_n"]
             assert coords.setdefault(t, (tm, tn)) == (tm, tn)
             assert 0 <= kb < ke <= p["k_iters"]
-            for k in range(kb, ke):
-                cover[(t, k)] += 1
+            assert nh in (-1, 0, 1)
+            if nh >= 0:
+                # half-width tiles: whole K, no partial-tile reduction
+                assert p["half"] == 1 and role == ROLE_FULL and (kb, ke) == (0, p["k_iters"])
+            # a whole tile covers both 128-column halves
+            for h in ((0, 1) if nh < 0 else (nh,)):
+                for k in range(kb, ke):
+                    cover[(t, h, k)] += 1
             if role == ROLE_CONTRIB:
                 # a unit contributes at most once, in its first stream-K segment
                 assert not seen_sk
@@ -71,7 +77,7 @@ def test_schedule_covers_every_iteration_once(options, shape, num_sms):
                 assert idx == len(items) - 1  # the owner's wait is its last item
             if t >= p["dp_tiles"]:
                 seen_sk = True
-    assert len(cover) == tiles * p["k_iters"]
+    assert len(cover) == 2 * tiles * p["k_iters"]
     assert all(v == 1 for v in cover.values())
     assert len(set(coords.values())) == tiles
     for t, units in contrib_of.items():
@@ -90,6 +96,25 @@ def test_default_plan_for_the_headline_config():
     p = ops.plan(_lib.KIND_MXFP4, 4096, 4096, 8192, 148)
     # 4096 bytes of packed K per row, in stages of two 128-byte chunks
     assert p["cta_group"] == 2 and p["units"] == 74 and p["k_iters"] == 16
-    # 16-stage tiles are not split (a piece must span 16 stages): the 34
-    # leftover tiles run whole, which beats split plus partial-tile fix-up
+    # 16-stage tiles are not split (a piece must span 16 stages)
     assert p["splits"] == 1
+
+
+@pytest.fixture
+def half_mode():
+    old = _lib.get_option(_lib.OPT_SK_MODE)
+    _lib.set_option(_lib.OPT_SK_MODE, 4)
+    yield
+    _lib.set_option(_lib.OPT_SK_MODE, old)
+
+
+def test_half_mode_plans(half_mode):
+    # 4096^2: the 34 leftover tiles as 68 half-width tiles on 68 pairs
+    p = ops.plan(_lib.KIND_F16, 4096, 4096, 8192, 148)
+    assert p["dp_tiles"] == 222 and p["half"] == 1 and p["sk_units"] == 68
+    # 3840^2: 225 tiles = 3 waves + 3 leftovers -> 6 half tiles fit
+    p = ops.plan(_lib.KIND_F16, 3840, 3840, 8192, 148)
+    assert p["half"] == 1 and p["sk_units"] == 6
+    # 50 leftover tiles (2 x 50 > 74 units): k-splits instead
+    p = ops.plan(_lib.KIND_F16, 256 * 11, 256 * 11, 8192, 148)   # 121 tiles = 74 + 47
+    assert p["dp_tiles"] == 74 and p["half"] == 0 and p["splits"] >= 1

@@ -15,15 +15,19 @@ pytestmark = pytest.mark.gpu
 
 
 def test_injected_flag_wait_times_out_and_context_recovers(cuda_device):
-    keys = (_lib.OPT_INJECT_FLAG_TIMEOUT, _lib.OPT_TIMEOUT_MS, _lib.OPT_MIN_SK_ITERS)
+    keys = (_lib.OPT_INJECT_FLAG_TIMEOUT, _lib.OPT_TIMEOUT_MS, _lib.OPT_MIN_SK_ITERS,
+            _lib.OPT_SK_MODE)
     old = {k: _lib.get_option(k) for k in keys}
-    M, N, K = 512, 512, 4096   # 4 pair tiles on 74 pairs: every tile is split (stream-K)
+    M, N, K = 512, 512, 4096   # 4 pair tiles on 74 pairs: every tile is split in k
     a = torch.randn((M, K), device="cuda", dtype=torch.float16)
     b_t = torch.randn((N, K), device="cuda", dtype=torch.float16)
-    p = ops.plan(_lib.KIND_F16, M, N, K, torch.cuda.get_device_properties(0).multi_processor_count)
-    assert p["sk_units"] > 1, p
     try:
+        # split mode: the leftover tiles have owners that wait for contributors
+        _lib.set_option(_lib.OPT_SK_MODE, 3)
         _lib.set_option(_lib.OPT_MIN_SK_ITERS, 1)
+        p = ops.plan(_lib.KIND_F16, M, N, K,
+                     torch.cuda.get_device_properties(0).multi_processor_count)
+        assert p["splits"] > 1, p
         _lib.set_option(_lib.OPT_TIMEOUT_MS, 200)
         _lib.set_option(_lib.OPT_INJECT_FLAG_TIMEOUT, 1)
         ops.gemm_f16(a, b_t)
