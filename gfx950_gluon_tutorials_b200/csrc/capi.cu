@@ -848,10 +848,11 @@ int b2g_plan_items(int kind, int M, int N, int K, int num_sms, int unit, int32_t
   int n = 0;
   while (cursor_next(g.plan, unit, cur, w)) {
     if (items != nullptr && n < max_items) {
-      int32_t* o = items + 10 * n;
+      int32_t* o = items + 11 * n;
       o[0] = w.tile; o[1] = w.tm; o[2] = w.tn; o[3] = w.k_begin; o[4] = w.k_end;
       o[5] = w.role; o[6] = w.first_contrib; o[7] = w.n_contrib; o[8] = w.contrib_stride;
       o[9] = w.nh;
+      o[10] = w.pair_half;
     }
     ++n;
   }

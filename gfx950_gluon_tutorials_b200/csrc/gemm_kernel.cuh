@@ -717,8 +717,15 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
       const int32_t m0 = w.tm * (128 * CG) + static_cast<int32_t>(rank) * 128 + quad * 32;
       const bool half = w.nh >= 0;  // a half-width tile fills chunks 0-3 only
       const int32_t n0 = w.tn * 256 + (half ? w.nh * 128 : 0);
-      // with overlapping accumulators the shared chunks are drained first
-      const uint32_t first_chunk = kScaled ? (b == 0 ? 8u - SP::kOvlChunks : 0u) : 0u;
+      // With overlapping accumulators the shared chunks are drained first. A
+      // piece of a two-piece split tile (always its unit's last item, so no
+      // later tile waits for particular columns) starts with the four chunks
+      // it hands to its peer: chunks pub_lo .. pub_lo + 3 are published, then
+      // the other four reduced and stored.
+      const uint32_t pub_lo = w.pair_half == 0 ? 4u : 0u;
+      const uint32_t first_chunk =
+          w.role == kRolePair ? pub_lo : (kScaled ? (b == 0 ? 8u - SP::kOvlChunks : 0u) : 0u);
+      bool pair_ok = true;
       // A split item that is this unit's last one finds the operand ring idle
       // (all its loads were consumed): each epilogue warp then moves its 32 x
       // 256 fp32 partial through its own 32 KB of the ring with bulk TMA copies
@@ -755,35 +762,137 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
         }
         if (!fok) break;
       }
-      // The chunks shared with the other accumulator go to registers first and
-      // are released at once, so the next tile's MMAs wait for three TMEM loads
-      // rather than for the conversion and stores of the chunks before them.
-      constexpr uint32_t kPre = kScaled ? SP::kOvlChunks : 0u;
-      uint32_t pre[kPre > 0 ? kPre : 1][32];
-      if constexpr (kPre > 0) {
-#pragma unroll
-        for (uint32_t k = 0; k < kPre; ++k)
-          tmem_ld_32x32b_x32(tbase + ((first_chunk + k) & 7u) * 32u, pre[k]);
-        tmem_wait_ld();
-#pragma unroll
-        for (uint32_t k = 0; k < kPre; ++k) tmem_regs_ready(pre[k]);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) {
-          if constexpr (CG == 1)
-            mbar_arrive(ovl_bar);
-          else
-            mbar_arrive_remote_relaxed(map_to_cta(ovl_bar, 0));
-        }
-      }
       // A unit's last tile stages all eight of its output chunks in the idle
       // operand ring (beyond the 128 KB the split-tile partials may occupy),
       // so its TMA stores go out back to back without waiting for one another.
       uint8_t* const stage_last = smem + 131072u + quad * 16384u;
+      // Convert and stage 32 rows x 32 columns in the 64-byte swizzle, then
+      // one TMA store per warp (the tensor map clips rows / columns past C).
+      // Chunks wholly outside C are skipped without touching the staging
+      // buffers. Other tiles alternate two buffers per store actually issued:
+      // the buffer being written is never the one the newest store may still
+      // be reading.
+      auto store_c = [&](uint32_t c, const uint32_t (&v)[32]) {
+        const int32_t x = n0 + static_cast<int32_t>(c * 32u);
+        if (x >= p.N || m0 >= p.M) return;
+        uint8_t* buf;
+        if (last_item) {
+          buf = stage_last + c * SP::kEpiBufBytes;
+        } else {
+          buf = stage_base + (nstore & 1u) * SP::kEpiBufBytes;
+          if (lane == 0) bulk_wait_group_read<1>();
+          __syncwarp();
+        }
+#pragma unroll
+        for (uint32_t pc = 0; pc < 4; ++pc) {
+          uint4 q4;
+          q4.x = pack_out<OUT_BF16>(v[8 * pc + 0], v[8 * pc + 1]);
+          q4.y = pack_out<OUT_BF16>(v[8 * pc + 2], v[8 * pc + 3]);
+          q4.z = pack_out<OUT_BF16>(v[8 * pc + 4], v[8 * pc + 5]);
+          q4.w = pack_out<OUT_BF16>(v[8 * pc + 6], v[8 * pc + 7]);
+          const uint32_t off = lane * 64u + ((pc ^ ((lane >> 1) & 3u)) << 4);
+          *reinterpret_cast<uint4*>(buf + off) = q4;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&p.tmC, smem_u32(buf), x, m0);
+          bulk_commit_group();
+        }
+        ++nstore;
+      };
       // One 32-column chunk: the split-tile part, then convert, stage and store.
       auto body = [&](uint32_t ci, uint32_t (&v)[32]) {
         const uint32_t c = (first_chunk + ci) & 7u;
         if (half && c >= 4u) return;
+        if (w.role == kRolePair) {
+          if (!pair_ok) return;
+          const int32_t peer = w.first_contrib;
+          if (ci < 4u) {
+            // the peer's half: this piece's fp32 partial
+            if (ring_fix) {
+              // 32 rows x 32 fp32 in the 128-byte swizzle, one box per chunk
+              uint8_t* box = ring + ci * 4096u + lane * 128u;
+#pragma unroll
+              for (uint32_t q = 0; q < 8; ++q)
+                *reinterpret_cast<uint4*>(box + ((q ^ (lane & 7u)) << 4)) =
+                    make_uint4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+            } else {
+              float4* dst = reinterpret_cast<float4*>(p.partials + partial_slot(unit, rank, CG) +
+                                                      static_cast<size_t>(row) * 256u + c * 32u);
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                __stcg(dst + i,
+                       make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                                   __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3])));
+            }
+            if (ci < 3u) return;
+            // all four published: raise this piece's flag, then take the peer's
+            // partial of this piece's half (its flag) into the ring's upper 16 KB
+            if (ring_fix) {
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                const int32_t y = (unit * CG + static_cast<int32_t>(rank)) * 128 +
+                                  static_cast<int32_t>(quad) * 32;
+                for (uint32_t j = 0; j < 4; ++j)
+                  tma_store_2d(&p.tmP, smem_u32(ring + j * 4096u),
+                               static_cast<int32_t>(((pub_lo + j) & 7u) * 32u), y);
+                bulk_commit_group();
+                bulk_wait_group<0>();   // partial written to global memory
+                fence_proxy_async_all();
+              }
+            } else {
+              __threadfence();
+            }
+            __syncwarp();
+            if (lane == 0) st_release_gpu(p.flags + flag_index(unit, rank, quad, CG), 1u);
+            bool fok = wait_flag(p.flags + flag_index(peer, rank, quad, CG), p.inject ? 2u : 1u,
+                                 abort_flag, p, B2G_SITE_FLAG);
+            fok = __all_sync(0xffffffffu, fok);
+            if (fok && ring_fix) {
+              fence_proxy_async_all();  // partials seen by the flag acquire -> TMA reads
+              if (lane == 0) {
+                mbar_arrive_expect_tx(fix_bar(quad), 4u * 4096u);
+                const int32_t y = (peer * CG + static_cast<int32_t>(rank)) * 128 +
+                                  static_cast<int32_t>(quad) * 32;
+                for (uint32_t j = 0; j < 4; ++j)
+                  tma_load_2d(smem_u32(ring + 16384u + j * 4096u), &p.tmP, fix_bar(quad),
+                              static_cast<int32_t>(((pub_lo + 4u + j) & 7u) * 32u), y);
+              }
+              fok = wait_phase<false>(fix_bar(quad), 0, abort_flag, p, B2G_SITE_FLAG);
+              fok = __all_sync(0xffffffffu, fok);
+            }
+            pair_ok = fok;
+            return;
+          }
+          // this piece's half: own accumulator + the peer's partial
+          if (ring_fix) {
+            const uint8_t* box = ring + 16384u + (ci - 4u) * 4096u + lane * 128u;
+#pragma unroll
+            for (uint32_t q = 0; q < 8; ++q) {
+              const float4 t = *reinterpret_cast<const float4*>(box + ((q ^ (lane & 7u)) << 4));
+              v[4 * q + 0] = __float_as_uint(__uint_as_float(v[4 * q + 0]) + t.x);
+              v[4 * q + 1] = __float_as_uint(__uint_as_float(v[4 * q + 1]) + t.y);
+              v[4 * q + 2] = __float_as_uint(__uint_as_float(v[4 * q + 2]) + t.z);
+              v[4 * q + 3] = __float_as_uint(__uint_as_float(v[4 * q + 3]) + t.w);
+            }
+          } else {
+            const float4* src = reinterpret_cast<const float4*>(
+                p.partials + partial_slot(peer, rank, CG) + static_cast<size_t>(row) * 256u +
+                c * 32u);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float4 t = __ldcg(src + i);
+              v[4 * i + 0] = __float_as_uint(__uint_as_float(v[4 * i + 0]) + t.x);
+              v[4 * i + 1] = __float_as_uint(__uint_as_float(v[4 * i + 1]) + t.y);
+              v[4 * i + 2] = __float_as_uint(__uint_as_float(v[4 * i + 2]) + t.z);
+              v[4 * i + 3] = __float_as_uint(__uint_as_float(v[4 * i + 3]) + t.w);
+            }
+          }
+          store_c(c, v);
+          return;
+        }
         if (w.role == kRoleContrib) {
           if (ring_fix) {
             // 32 rows x 32 fp32 in the 128-byte swizzle, one box per chunk
@@ -819,89 +928,71 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
             const float4* src = reinterpret_cast<const float4*>(
                 p.partials + partial_slot(u2, rank, CG) + static_cast<size_t>(row) * 256u +
                 c * 32u);
-            float4 t[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) t[i] = __ldcg(src + i);
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-              v[4 * i + 0] = __float_as_uint(__uint_as_float(v[4 * i + 0]) + t[i].x);
-              v[4 * i + 1] = __float_as_uint(__uint_as_float(v[4 * i + 1]) + t[i].y);
-              v[4 * i + 2] = __float_as_uint(__uint_as_float(v[4 * i + 2]) + t[i].z);
-              v[4 * i + 3] = __float_as_uint(__uint_as_float(v[4 * i + 3]) + t[i].w);
+              const float4 t = __ldcg(src + i);
+              v[4 * i + 0] = __float_as_uint(__uint_as_float(v[4 * i + 0]) + t.x);
+              v[4 * i + 1] = __float_as_uint(__uint_as_float(v[4 * i + 1]) + t.y);
+              v[4 * i + 2] = __float_as_uint(__uint_as_float(v[4 * i + 2]) + t.z);
+              v[4 * i + 3] = __float_as_uint(__uint_as_float(v[4 * i + 3]) + t.w);
             }
           }
         }
-        // Convert and stage 32 rows x 32 columns in the 64-byte swizzle, then
-        // one TMA store per warp (the tensor map clips rows / columns past C).
-        // Chunks wholly outside C are skipped without touching the staging
-        // buffers. Other tiles alternate two buffers per store actually
-        // issued: the buffer being written is never the one the newest store
-        // may still be reading.
-        const int32_t x = n0 + static_cast<int32_t>(c * 32u);
-        if (x >= p.N || m0 >= p.M) return;
-        uint8_t* buf;
-        if (last_item) {
-          buf = stage_last + c * SP::kEpiBufBytes;
-        } else {
-          buf = stage_base + (nstore & 1u) * SP::kEpiBufBytes;
-          if (lane == 0) bulk_wait_group_read<1>();
-          __syncwarp();
-        }
+        store_c(c, v);
+      };
+      // The chunks shared with the other accumulator go to registers first and
+      // are released at once, so the next tile's MMAs wait for three TMEM loads
+      // rather than for the conversion and stores of the chunks before them.
+      constexpr uint32_t kPre = kScaled ? SP::kOvlChunks : 0u;
+      uint32_t pre[kPre > 0 ? kPre : 1][32];
+      if constexpr (kPre > 0) {
 #pragma unroll
-        for (uint32_t pc = 0; pc < 4; ++pc) {
-          uint4 q4;
-          q4.x = pack_out<OUT_BF16>(v[8 * pc + 0], v[8 * pc + 1]);
-          q4.y = pack_out<OUT_BF16>(v[8 * pc + 2], v[8 * pc + 3]);
-          q4.z = pack_out<OUT_BF16>(v[8 * pc + 4], v[8 * pc + 5]);
-          q4.w = pack_out<OUT_BF16>(v[8 * pc + 6], v[8 * pc + 7]);
-          const uint32_t off = lane * 64u + ((pc ^ ((lane >> 1) & 3u)) << 4);
-          *reinterpret_cast<uint4*>(buf + off) = q4;
-        }
-        fence_proxy_async_smem();
+        for (uint32_t k = 0; k < kPre; ++k)
+          tmem_ld_32x32b_x32(tbase + ((first_chunk + k) & 7u) * 32u, pre[k]);
+        tmem_wait_ld();
+#pragma unroll
+        for (uint32_t k = 0; k < kPre; ++k) tmem_regs_ready(pre[k]);
+        tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(&p.tmC, smem_u32(buf), x, m0);
-          bulk_commit_group();
+          if constexpr (CG == 1)
+            mbar_arrive(ovl_bar);
+          else
+            mbar_arrive_remote_relaxed(map_to_cta(ovl_bar, 0));
         }
-        ++nstore;
-      };
-      // Chunk ci's values in v: from the registers the overlap drain filled,
-      // or from the TMEM load issued one chunk earlier (fetch).
+      }
+      // The drained chunks first, with compile-time indices so that each set of
+      // registers dies once used; the first TMEM chunk after them is already
+      // loading. Then two register buffers: the next chunk's TMEM load is in
+      // flight while the current one is converted and stored.
       auto fetch = [&](uint32_t ci, uint32_t (&v)[32]) {
         tmem_ld_32x32b_x32(tbase + ((first_chunk + ci) & 7u) * 32u, v);
       };
-      auto in_pre = [](uint32_t ci) {
-        if constexpr (kPre == 0) return false;
-        else return ci < kPre;
+      auto ready = [&](uint32_t (&v)[32]) {
+        tmem_wait_ld();
+        tmem_regs_ready(v);
       };
-      auto take = [&](uint32_t ci, uint32_t (&v)[32]) {
-        if (in_pre(ci)) {
-          if constexpr (kPre > 0) {
-#pragma unroll
-            for (uint32_t k = 0; k < kPre; ++k)
-              if (ci == k) {
-#pragma unroll
-                for (int i = 0; i < 32; ++i) v[i] = pre[k][i];
-              }
-          }
-        } else {
-          tmem_wait_ld();
-          tmem_regs_ready(v);
-        }
-      };
-      // Two register buffers: the next chunk's TMEM load is in flight while
-      // the current one is converted and stored.
       uint32_t va[32], vb[32];
-      if constexpr (kPre == 0) fetch(0, va);
+      fetch(kPre, va);
+      if constexpr (kPre > 0) {
+#pragma unroll
+        for (uint32_t k = 0; k < kPre; ++k) body(k, pre[k]);
+      }
+      uint32_t ci = kPre;
 #pragma unroll 1
-      for (uint32_t ci = 0; ci < 8; ci += 2) {
-        take(ci, va);
-        if (!in_pre(ci + 1)) fetch(ci + 1, vb);
+      for (; ci + 1 < 8u; ci += 2) {
+        ready(va);
+        fetch(ci + 1, vb);
         body(ci, va);
-        take(ci + 1, vb);
-        if (ci + 2 < 8 && !in_pre(ci + 2)) fetch(ci + 2, va);
+        ready(vb);
+        if (ci + 2 < 8u) fetch(ci + 2, va);
         body(ci + 1, vb);
       }
+      if (ci < 8u) {
+        ready(va);
+        body(ci, va);
+      }
+      if (!pair_ok) break;
       if (w.role == kRoleContrib) {
         if (ring_fix) {
           fence_proxy_async_smem();
@@ -920,7 +1011,8 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
         }
         __syncwarp();
         if (lane == 0) st_release_gpu(p.flags + flag_index(unit, rank, quad, CG), 1u);
-      } else if (w.role == kRoleOwner) {
+      } else if (w.role == kRoleOwner || w.role == kRolePair) {
+        // the contributors' (the peer's) flags have been consumed: zero at rest
         __syncwarp();
         if (lane == 0)
           for (int32_t ci2 = 0, u2 = w.first_contrib; ci2 < w.n_contrib;

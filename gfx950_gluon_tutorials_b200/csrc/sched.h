@@ -20,12 +20,19 @@
 //     K) on units 2j and 2j + 1. An N = 128 MMA takes half the time of an
 //     N = 256 one, so the last wave takes about half a tile and needs no
 //     partial-tile reduction; otherwise mode 4 falls back to mode 3.
-// Ownership rule (both): the unit that runs k-iteration 0 of a split tile
-// owns it. Every other unit touching the tile does so in the FIRST segment of
-// its range, writes an fp32 partial to its own workspace slot and raises a
-// flag; the owner adds the partials in increasing unit order (deterministic)
-// after its own accumulation and stores C. Contributors never wait and always
-// have larger unit numbers than the owner, so the waits cannot form a cycle.
+// Ownership rule (stream-K, and splits into more than two pieces): the unit
+// that runs k-iteration 0 of a split tile owns it. Every other unit touching
+// the tile does so in the FIRST segment of its range, writes an fp32 partial
+// to its own workspace slot and raises a flag; the owner adds the partials in
+// increasing unit order (deterministic) after its own accumulation and stores
+// C. Contributors never wait and always have larger unit numbers than the
+// owner, so the waits cannot form a cycle.
+// Pair rule (a tile split into two pieces): each piece reduces half of the
+// tile's columns. Piece s keeps columns [128 s, 128 s + 128): it publishes its
+// partial of the other half, raises its flag, then waits for its peer's flag
+// and adds the peer's partial of its own half (peer partial + own, in that
+// order on both sides: deterministic). Both publish before waiting, so the
+// waits cannot form a cycle, and the two halves are reduced in parallel.
 #pragma once
 
 #include <stdint.h>
@@ -38,7 +45,7 @@
 
 namespace b2g {
 
-enum : int { kRoleFull = 0, kRoleOwner = 1, kRoleContrib = 2 };
+enum : int { kRoleFull = 0, kRoleOwner = 1, kRoleContrib = 2, kRolePair = 3 };
 
 struct SkPlan {
   int32_t tiles_m, tiles_n;  // output tile grid
@@ -61,6 +68,8 @@ struct WorkItem {
   // owner only: contributing units first, first + stride, ... (n_contrib of them)
   int32_t first_contrib, n_contrib, contrib_stride;
   int32_t nh;        // -1: whole tile; 0 / 1: columns [0, 128) / [128, 256) of the tile
+  // pair only: the half this piece reduces (0 / 1); its peer is first_contrib
+  int32_t pair_half;
 };
 
 B2G_HD int32_t plan_tiles(const SkPlan& p) { return p.tiles_m * p.tiles_n; }
@@ -164,6 +173,7 @@ B2G_HD bool cursor_next(const SkPlan& p, int32_t u, WorkCursor& c, WorkItem& w) 
   w.n_contrib = 0;
   w.contrib_stride = 1;
   w.nh = -1;
+  w.pair_half = -1;
   if (c.dp_next < p.dp_tiles) {
     w.tile = c.dp_next;
     w.k_begin = 0;
@@ -194,6 +204,11 @@ B2G_HD bool cursor_next(const SkPlan& p, int32_t u, WorkCursor& c, WorkItem& w) 
     w.k_end = static_cast<int32_t>((static_cast<int64_t>(p.k_iters) * (s + 1)) / p.splits);
     if (p.splits == 1) {
       w.role = kRoleFull;
+    } else if (p.splits == 2) {
+      w.role = kRolePair;
+      w.pair_half = s;
+      w.first_contrib = s == 0 ? u + left : u - left;
+      w.n_contrib = 1;
     } else if (s == 0) {
       w.role = kRoleOwner;
       w.first_contrib = u + left;

@@ -371,14 +371,15 @@ def plan(kind: int, M: int, N: int, K: int, num_sms: int = 148) -> dict:
 
 def plan_items(kind: int, M: int, N: int, K: int, unit: int, num_sms: int = 148) -> list[tuple]:
     """Work items (tile, tm, tn, k_begin, k_end, role, first_contrib, n_contrib,
-    contrib_stride, nh) of one unit; nh is -1 for a whole tile, 0 / 1 for the
-    first / second 128 columns of a half-width tile."""
+    contrib_stride, nh, pair_half) of one unit; nh is -1 for a whole tile, 0 / 1
+    for the first / second 128 columns of a half-width tile; pair_half is the
+    column half a piece of a two-piece split tile reduces (role 3), else -1."""
     n = lib().b2g_plan_items(kind, M, N, K, num_sms, unit, None, 0)
     if n < 0:
         check(n, "b2g_plan_items")
-    buf = (ctypes.c_int32 * (10 * max(n, 1)))()
+    buf = (ctypes.c_int32 * (11 * max(n, 1)))()
     lib().b2g_plan_items(kind, M, N, K, num_sms, unit, buf, n)
-    return [tuple(buf[10 * i:10 * i + 10]) for i in range(n)]
+    return [tuple(buf[11 * i:11 * i + 11]) for i in range(n)]
 
 
 __all__ = [

@@ -278,11 +278,13 @@ B2G_API int64_t b2g_get_option(int key);
  * dp_tiles, sk_units, launched_units, group_m, splits, half}; out_len >= 11. */
 B2G_API int b2g_plan_query(int kind, int M, int N, int K, int num_sms, int32_t* out, int out_len);
 
-/* Work items of one unit in execution order, 10 ints each: {tile, tm, tn,
- * k_begin, k_end, role (0 full, 1 split-tile owner, 2 contributor),
- * first_contrib, n_contrib, contrib_stride, nh (-1 whole tile, 0 / 1 first /
- * second 128 columns of a half-width tile)}. Returns the item count (items
- * may be NULL). */
+/* Work items of one unit in execution order, 11 ints each: {tile, tm, tn,
+ * k_begin, k_end, role (0 full, 1 split-tile owner, 2 contributor, 3 one of
+ * the two pieces of a tile split in two), first_contrib (for role 3: the other
+ * piece's unit), n_contrib, contrib_stride, nh (-1 whole tile, 0 / 1 first /
+ * second 128 columns of a half-width tile), pair_half (role 3: the column
+ * half this piece reduces, else -1)}. Returns the item count (items may be
+ * NULL). */
 B2G_API int b2g_plan_items(int kind, int M, int N, int K, int num_sms, int unit, int32_t* items,
                    int max_items);
 

@@ -11,7 +11,7 @@ import pytest
 
 from gfx950_gluon_tutorials_b200 import _lib, ops
 
-ROLE_FULL, ROLE_OWNER, ROLE_CONTRIB = 0, 1, 2
+ROLE_FULL, ROLE_OWNER, ROLE_CONTRIB, ROLE_PAIR = 0, 1, 2, 3
 
 SHAPES = [
     (_lib.KIND_F16, 4096, 4096, 8192),     # 256 pair tiles over 74 pairs
@@ -49,11 +49,12 @@ def test_schedule_covers_every_iteration_once(options, shape, num_sms):
     cover = defaultdict(int)
     owners = {}
     contrib_of = defaultdict(list)
+    pairs = defaultdict(list)
     coords = {}
     for u in range(p["launched"]):
         items = ops.plan_items(kind, M, N, K, u, num_sms)
         seen_sk = False
-        for idx, (t, tm, tn, kb, ke, role, first, n_c, stride, nh) in enumerate(items):
+        for idx, (t, tm, tn, kb, ke, role, first, n_c, stride, nh, ph) in enumerate(items):
             assert 0 <= t < tiles and 0 <= tm < p["tiles_m"] and 0 <= tn < p["tiles_n"]
             assert coords.setdefault(t, (tm, tn)) == (tm, tn)
             assert 0 <= kb < ke <= p["k_iters"]
@@ -75,6 +76,12 @@ def test_schedule_covers_every_iteration_once(options, shape, num_sms):
                 assert t not in owners
                 owners[t] = (u, [first + i * stride for i in range(n_c)])
                 assert idx == len(items) - 1  # the owner's wait is its last item
+            if role == ROLE_PAIR:
+                # one of two pieces: the unit's last item, naming its peer
+                assert p["splits"] == 2 and ph in (0, 1) and idx == len(items) - 1
+                pairs[t].append((u, ph, first, kb, ke))
+            else:
+                assert ph == -1
             if t >= p["dp_tiles"]:
                 seen_sk = True
     assert len(cover) == 2 * tiles * p["k_iters"]
@@ -85,6 +92,12 @@ def test_schedule_covers_every_iteration_once(options, shape, num_sms):
         assert sorted(units) == listed
         assert u < min(listed)
     assert set(owners) == set(contrib_of)
+    for t, pieces in pairs.items():
+        # the two pieces keep complementary column halves and name each other
+        assert len(pieces) == 2
+        (u0, h0, peer0, kb0, ke0), (u1, h1, peer1, kb1, ke1) = sorted(pieces, key=lambda x: x[1])
+        assert (h0, h1) == (0, 1) and peer0 == u1 and peer1 == u0
+        assert kb0 == 0 and ke0 == kb1 and ke1 == p["k_iters"]
 
 
 def test_default_plan_for_the_headline_config():
