@@ -15,11 +15,13 @@
 //     s of leftover tile j goes to unit s * leftover + j, so units running at
 //     the same time stream the same k-range of neighbouring tiles (their A and
 //     B panels stay shared in L2, which contiguous ranges lose);
-//   half (mode 4, when twice the leftover tiles fit on the units): every
+//   half (mode 4, and mode 3 when the tiles are too short to split in K;
+//     both only when twice the leftover tiles fit on the units): every
 //     leftover tile runs as two independent half-width tiles (N = 128, whole
-//     K) on units 2j and 2j + 1. An N = 128 MMA takes half the time of an
-//     N = 256 one, so the last wave takes about half a tile and needs no
-//     partial-tile reduction; otherwise mode 4 falls back to mode 3.
+//     K) on units 2j and 2j + 1, with no partial-tile reduction. An N = 128
+//     MMA takes half the time of an N = 256 one, but a half tile still loads
+//     its whole A panel, so it takes well over half a tile: splitting in K
+//     (same bytes shared by two units) is preferred where a tile is long.
 // Ownership rule (stream-K, and splits into more than two pieces): the unit
 // that runs k-iteration 0 of a split tile owns it. Every other unit touching
 // the tile does so in the FIRST segment of its range, writes an fp32 partial
@@ -134,6 +136,13 @@ inline SkPlan make_plan(int32_t tiles_m, int32_t tiles_n, int32_t k_iters, int32
     if (s > s_max) s = s_max;
     if (s > kMaxSplits) s = kMaxSplits;
     if (s < 1) s = 1;
+    if (s == 1 && 2 * left <= units) {
+      // too short to split in K (MXFP4 at K = 8192: 16 stages): half-width
+      // tiles still put the idle units to work (58.3 against 59.3 us)
+      p.half = 1;
+      p.sk_units = 2 * left;
+      return p;
+    }
     p.splits = s;
     p.sk_units = left * s;
     return p;

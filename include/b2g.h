@@ -249,10 +249,11 @@ B2G_API int b2g_cast_e5m2(const void* src, int src_dtype, int64_t n, uint8_t* ds
                                  0: run as a partial wave; 1: stream-K (equal
                                  contiguous (tile, k) ranges per unit); 2: stream-K
                                  over the last full wave plus the partial one;
-                                 3 (default): split each into equal k-chunks;
-                                 4: run each as two half-width (N = 128) tiles
-                                 when twice their count fits on the units, else
-                                 as 3 */
+                                 3 (default): split each into two k-pieces
+                                 (each piece reduces half of the tile), or, when
+                                 the tiles are too short to split, run each as
+                                 two half-width (N = 128) tiles if they fit;
+                                 4: half-width tiles whenever they fit, else as 3 */
 #define B2G_OPT_GROUP_M 3     /* raster group height in tiles (default 1: row-major) */
 #define B2G_OPT_MIN_SK_ITERS 4 /* minimum k-iterations (256-byte stages) per stream-K unit
                                   or split piece (default 16) */

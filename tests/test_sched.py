@@ -109,8 +109,9 @@ def test_default_plan_for_the_headline_config():
     p = ops.plan(_lib.KIND_MXFP4, 4096, 4096, 8192, 148)
     # 4096 bytes of packed K per row, in stages of two 128-byte chunks
     assert p["cta_group"] == 2 and p["units"] == 74 and p["k_iters"] == 16
-    # 16-stage tiles are not split (a piece must span 16 stages)
-    assert p["splits"] == 1
+    # 16-stage tiles are too short to split (a piece must span 16 stages):
+    # the 34 leftover tiles run as 68 half-width tiles instead
+    assert p["splits"] == 0 and p["half"] == 1 and p["sk_units"] == 68
 
 
 @pytest.fixture
