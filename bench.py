@@ -574,7 +574,8 @@ def time_gemm_gather(w: Workload, world: int, iters: int, chunks: int = 4) -> di
     (GEMM, then the NCCL all-gather) against `shard.gemm_gather_p2p` (row
     chunks written into a symmetric buffer, each chunk copied to the peers by
     the copy engines while the next chunk computes)."""
-    from gfx950_gluon_tutorials_b200.shard import gather_slabs, gemm_gather_p2p
+    from gfx950_gluon_tutorials_b200.shard import (P2P_MAX_WORLD, gather_slabs, gemm_gather,
+                                                   gemm_gather_p2p)
     ops = w.ops
     s = w.sets[0]
     copy = torch.cuda.Stream()
@@ -599,8 +600,13 @@ def time_gemm_gather(w: Workload, world: int, iters: int, chunks: int = 4) -> di
         torch.cuda.synchronize()
         return max_over_ranks(start.elapsed_time(end) / iters, world)
 
+    def chosen():
+        return gemm_gather(lambda x, y, out: ops.gemm_f16(x, y, out), s["a"], s["b"],
+                           chunks=chunks, out_dtype=s["c"].dtype, copy_stream=copy)
+
     seq = timed(sequential)
     ovl = timed(overlapped)
+    auto = timed(chosen)
     ops.check_status()
     # parity of the peer copies: every slot of this rank's buffer equals the
     # NCCL all-gather of the slabs each rank computed into its own slot
@@ -611,6 +617,9 @@ def time_gemm_gather(w: Workload, world: int, iters: int, chunks: int = 4) -> di
     ok = torch.tensor([1 if torch.equal(ref, buf) else 0], device=buf.device)
     torch.distributed.all_reduce(ok, op=torch.distributed.ReduceOp.MIN)
     return {"gemm_then_gather_ms": seq, "gemm_gather_p2p_overlapped_ms": ovl,
+            "gemm_gather_ms": auto,
+            "gemm_gather_path": ("p2p overlap" if world <= P2P_MAX_WORLD
+                                 else "GEMM then NCCL all-gather"),
             "overlap_chunks": chunks, "gather_parity_ok": bool(ok.item() == 1),
             "gather_parity_check": "p2p-gathered [world][M][n] buffer equals the NCCL "
                                    "all-gather of each rank's own slot (torch.equal)"}

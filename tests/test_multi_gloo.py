@@ -99,3 +99,54 @@ def test_chunk_rows_cover_whole_tiles(m, chunks):
     for (lo, hi), (lo2, _) in zip(pieces, pieces[1:]):
         assert hi == lo2 and lo % 256 == 0
     assert len(pieces) <= chunks
+
+
+def _gather_worker(rank, world, port, queue):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    from gfx950_gluon_tutorials_b200 import shard
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=20))
+    try:
+        g = torch.Generator().manual_seed(0)
+        M, N, K = 64, 256 * world, 96
+        a = torch.randn(M, K, generator=g)
+        b = torch.randn(N, K, generator=g)
+        lo, hi = shard.shard_range(N, world, rank)
+        shard.P2P_MAX_WORLD = 1   # above it: the GEMM-then-gather path (no GPU needed)
+
+        def matmul(x, y, out):
+            out.copy_(x @ y.T)
+            return out
+
+        slabs = shard.gemm_gather(matmul, a, b[lo:hi], out_dtype=torch.float32)
+        ok = tuple(slabs.shape) == (world, M, hi - lo) and torch.allclose(
+            shard.assemble(slabs), a @ b.T, atol=1e-4, rtol=1e-4)
+        queue.put((rank, "ok" if ok else "mismatch"))
+    except Exception as e:  # noqa: BLE001
+        queue.put((rank, f"error: {e}"))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gemm_gather_large_world_path_gathers_every_slab():
+    """Above P2P_MAX_WORLD ranks, `gemm_gather` runs the whole slab GEMM and
+    then the all-gather; every rank ends with all slabs in rank order."""
+    world = 3
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gather_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    out = {}
+    while not q.empty():
+        r, msg = q.get()
+        out[r] = msg
+    assert out == {r: "ok" for r in range(world)}
