@@ -134,10 +134,10 @@ int64_t row_bytes(int kind, int64_t K) {
 
 size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
 
-// Zero-at-rest flag words at the start of every workspace: four per SM.
-size_t flag_region_bytes(int sms) {
-  return align256(static_cast<size_t>(sms) * 4 * sizeof(uint32_t));
-}
+// Zero-at-rest flag words at the start of every workspace: four per SM
+// (split-tile flags; the small-M kernel's per-tile counters).
+size_t flag_words(int sms) { return static_cast<size_t>(sms) * 4; }
+size_t flag_region_bytes(int sms) { return align256(flag_words(sms) * sizeof(uint32_t)); }
 
 struct Geometry {
   int cg;
@@ -196,10 +196,12 @@ Geometry geometry(int kind, int M, int N, int K, int sms, int pair_cap = 0, int 
 }
 
 // ------------------------------------------------------- skinny (small M) --
-bool use_skinny(int kind, int M) {
+// Its per-tile arrival counters live in the flag region, one word per
+// 128-column tile: wider problems take the persistent kernel.
+bool use_skinny(int kind, int M, int N, int sms) {
   const int64_t lim = g_opt.skinny_max_m.load();
   return (kind == B2G_KIND_F16 || kind == B2G_KIND_BF16 || kind == B2G_KIND_E5M2) && lim > 0 &&
-         M <= lim && M <= 128;
+         M <= lim && M <= 128 && static_cast<size_t>((N + 127) / 128) <= flag_words(sms);
 }
 
 struct SkinnyGeom {
@@ -453,7 +455,8 @@ int run_gemm(const GemmCall& c, const Geometry* fixed = nullptr) {
   cudaGetDevice(&dev);
   const int sms = current_sms();
   if (sms <= 0) return B2G_ENODEVICE;
-  if (fixed == nullptr && c.groups == nullptr && use_skinny(c.kind, c.M)) return run_skinny(c, sms);
+  if (fixed == nullptr && c.groups == nullptr && use_skinny(c.kind, c.M, c.N, sms))
+    return run_skinny(c, sms);
   const int b_rows = c.groups != nullptr ? c.n_groups * c.N : c.N;
   const Geometry g = fixed != nullptr
                          ? *fixed
@@ -625,7 +628,7 @@ size_t b2g_gemm_workspace_bytes(int kind, int M, int N, int K) {
   cudaGetDevice(&dev);
   const int sms = current_sms();
   if (sms <= 0) return 0;
-  if (use_skinny(kind, M)) return skinny_geometry(kind, M, N, K, sms).total;
+  if (use_skinny(kind, M, N, sms)) return skinny_geometry(kind, M, N, K, sms).total;
   return geometry(kind, M, N, K, sms, pair_capacity(dev, sms)).total;
 }
 

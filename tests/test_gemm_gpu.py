@@ -564,6 +564,21 @@ def test_skinny_agrees_with_the_persistent_kernel(cuda_device):
     assert_close(as_f32(c_skinny), as_f32(c_main), TOL_F16, ref_atol=False)
 
 
+def test_small_m_wider_than_the_counter_region(skinny_on):
+    """The small-M kernel keeps one arrival counter per 128-column tile in the
+    workspace's flag region (four words per SM); a problem with more tiles than
+    that takes the persistent kernel and is still correct."""
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    M, N, K = 8, sms * 4 * 128 + 256, 128
+    g = torch.Generator(device="cuda").manual_seed(31)
+    a = torch.rand((M, K), generator=g, device="cuda").half() - 0.5
+    b_t = torch.rand((N, K), generator=g, device="cuda").half() - 0.5
+    c = ops.gemm_f16(a, b_t)
+    ops.check_status()
+    ref = a.float() @ b_t.float().T
+    assert_close(as_f32(c), ref.cpu().numpy(), TOL_F16)
+
+
 def test_flag_region_stays_zero_across_mixed_calls(cuda_device):
     """One workspace shared by calls of different kinds and geometries: the
     flag words at its start are zero after every call (unsplit scaled GEMMs,
