@@ -340,6 +340,108 @@ __global__ void __launch_bounds__(256) sf_relayout_kernel(RelayoutArgs a, Relayo
   }
 }
 
+// Scales with 16-byte aligned rows in either common storage: K-contiguous
+// (s1 = 1) or M-contiguous (s0 = 1, the reference's storage). One CTA per
+// (128-row block, 16 groups): the source tile (128 rows x 64 k-blocks) is read
+// with coalesced 16-byte loads into shared memory, then each warp writes one
+// 512-byte block. (A thread per output word loading straight from global
+// memory touches a separate 32-byte sector for every 1 or 4 useful bytes.)
+// K-contiguous: shared rows 17 words apart, so the 32 rows one output word
+// gathers sit in 32 different banks. M-contiguous: 64 k-rows of 128 bytes,
+// 144 bytes apart; an output word gathers one byte from each of 4 k-rows.
+// Rows and k-blocks past the matrix read as 127 (scale 1.0).
+constexpr int kRlGroups = 16;  // 4-scale groups per CTA (64 k-blocks)
+
+__device__ __forceinline__ bool rl_kmajor(const RelayoutArgs& t) {
+  return t.s1 == 1 && t.s0 % 16 == 0;
+}
+
+__global__ void __launch_bounds__(256) sf_relayout_tile_kernel(RelayoutArgs a, RelayoutArgs b,
+                                                               int32_t kscales, int32_t groups) {
+  grid_dependency_wait();
+  grid_launch_dependents();
+  __shared__ __align__(16) uint8_t sm[64 * 144];  // >= 128 rows x 17 words
+  const int32_t gchunks = (groups + kRlGroups - 1) / kRlGroups;
+  const int64_t blk = blockIdx.x;
+  const int32_t rbi = static_cast<int32_t>(blk / gchunks);
+  const int32_t gc = static_cast<int32_t>(blk - int64_t{rbi} * gchunks);
+  const bool is_a = rbi < a.row_blocks;
+  const RelayoutArgs& t = is_a ? a : b;
+  const int32_t rb = is_a ? rbi : rbi - a.row_blocks;
+  const int32_t k0 = gc * kRlGroups * 4;
+  const int64_t row0 = int64_t{rb} * 128;
+  auto byte_at = [&](int64_t row, int32_t k) -> uint32_t {
+    return (row < t.rows && k < kscales) ? __ldg(t.src + row * t.s0 + int64_t{k} * t.s1) : 127u;
+  };
+  if (rl_kmajor(t)) {
+    uint32_t* tile = reinterpret_cast<uint32_t*>(sm);
+    for (int32_t pc = threadIdx.x; pc < 128 * 4; pc += blockDim.x) {
+      const int32_t r = pc >> 2, k = k0 + 16 * (pc & 3);
+      const int64_t row = row0 + r;
+      uint32_t w[4];
+      if (row < t.rows && k + 16 <= kscales) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(t.src + row * t.s0 + k));
+        w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          w[i] = byte_at(row, k + 4 * i) | (byte_at(row, k + 4 * i + 1) << 8) |
+                 (byte_at(row, k + 4 * i + 2) << 16) | (byte_at(row, k + 4 * i + 3) << 24);
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) tile[r * 17 + 4 * (pc & 3) + i] = w[i];
+    }
+    __syncthreads();
+    for (int32_t o = threadIdx.x; o < kRlGroups * 32; o += blockDim.x) {
+      const int32_t gl = o >> 5, r0 = o & 31;  // one group per warp
+      const int32_t g = gc * kRlGroups + gl;
+      if (g >= groups) break;
+      const uint4 v = make_uint4(tile[r0 * 17 + gl], tile[(32 + r0) * 17 + gl],
+                                 tile[(64 + r0) * 17 + gl], tile[(96 + r0) * 17 + gl]);
+      *reinterpret_cast<uint4*>(t.dst + (int64_t{rb} * groups + g) * 512 + r0 * 16) = v;
+    }
+  } else {
+    for (int32_t pc = threadIdx.x; pc < 64 * 8; pc += blockDim.x) {
+      const int32_t kr = pc >> 3, k = k0 + kr;
+      const int64_t row = row0 + 16 * (pc & 7);
+      uint4 v;
+      if (k < kscales && row + 16 <= t.rows) {
+        v = __ldg(reinterpret_cast<const uint4*>(t.src + row + int64_t{k} * t.s1));
+      } else {
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          w[i] = byte_at(row + 4 * i, k) | (byte_at(row + 4 * i + 1, k) << 8) |
+                 (byte_at(row + 4 * i + 2, k) << 16) | (byte_at(row + 4 * i + 3, k) << 24);
+        v = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      *reinterpret_cast<uint4*>(sm + kr * 144 + 16 * (pc & 7)) = v;
+    }
+    __syncthreads();
+    for (int32_t o = threadIdx.x; o < kRlGroups * 32; o += blockDim.x) {
+      const int32_t gl = o >> 5, r0 = o & 31;
+      const int32_t g = gc * kRlGroups + gl;
+      if (g >= groups) break;
+      const uint8_t* col = sm + 4 * gl * 144 + r0;
+      uint32_t w[4];
+#pragma unroll
+      for (int r1 = 0; r1 < 4; ++r1)
+        w[r1] = uint32_t{col[32 * r1]} | (uint32_t{col[144 + 32 * r1]} << 8) |
+                (uint32_t{col[288 + 32 * r1]} << 16) | (uint32_t{col[432 + 32 * r1]} << 24);
+      *reinterpret_cast<uint4*>(t.dst + (int64_t{rb} * groups + g) * 512 + r0 * 16) =
+          make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+}
+
+// Operands the tiled kernel takes: absent, or K- / M-contiguous with
+// 16-byte aligned base and rows.
+static bool tile_layout(const RelayoutArgs& t) {
+  if (t.row_blocks == 0) return true;
+  if ((reinterpret_cast<uintptr_t>(t.src) & 15u) != 0) return false;
+  return (t.s1 == 1 && t.s0 % 16 == 0) || (t.s0 == 1 && t.s1 % 16 == 0);
+}
+
 // Enough CTAs to cover `work` items once (the block scheduler balances the
 // waves); the kernels' grid-stride loops only matter past the grid limit.
 static int grid_for(int64_t work, int threads) {
@@ -433,6 +535,14 @@ cudaError_t launch_sf_relayout(const uint8_t* sa, int64_t sa0, int64_t sa1, int 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (tile_layout(a) && tile_layout(b)) {
+    const int64_t blocks = (static_cast<int64_t>(a.row_blocks) + b.row_blocks) *
+                           ((groups + kRlGroups - 1) / kRlGroups);
+    if (blocks < (int64_t{1} << 31)) {
+      cfg.gridDim = dim3(static_cast<unsigned>(blocks), 1, 1);
+      return cudaLaunchKernelEx(&cfg, sf_relayout_tile_kernel, a, b, kscales, groups);
+    }
+  }
   const cudaError_t e = work < (int64_t{1} << 31)
                             ? cudaLaunchKernelEx(&cfg, sf_relayout_kernel<uint32_t>, a, b, kscales, groups)
                             : cudaLaunchKernelEx(&cfg, sf_relayout_kernel<int64_t>, a, b, kscales, groups);

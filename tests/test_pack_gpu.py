@@ -135,3 +135,53 @@ def test_quantize_mxfp4_nearest_grid_value_edges(cuda_device):
     x = torch.from_numpy(_edge_matrix(1024, 4096, 99)).cuda()
     q, s = ops.quantize_mxfp4(x)
     _check_nearest_e2m1(x, q, s)
+
+
+def _blocked_ref(s: np.ndarray) -> np.ndarray:
+    """The GEMM's blocked scale layout restated in numpy: for 128-row block rb
+    and 4-scale group g, 512 bytes at (rb * groups + g) * 512 whose byte
+    r0 * 16 + r1 * 4 + j is the scale of row 128 rb + 32 r1 + r0, k-block
+    4 g + j; rows and k-blocks past the matrix hold 127."""
+    rows, kb = s.shape
+    rbs, groups = (rows + 127) // 128, (kb + 3) // 4
+    full = np.full((rbs * 128, groups * 4), 127, np.uint8)
+    full[:rows, :kb] = s
+    # (rb, r1, r0, g, j) -> (rb, g, r0, r1, j)
+    t = full.reshape(rbs, 4, 32, groups, 4).transpose(0, 3, 2, 1, 4)
+    return np.ascontiguousarray(t).reshape(-1)
+
+
+@pytest.mark.parametrize("layout", ["k_contig", "k_contig_ragged", "k_contig_padded_rows",
+                                    "m_contig", "m_contig_rows_pad", "strided"])
+@pytest.mark.parametrize("rows,K", [(4096, 8192), (300, 8192), (300, 2080), (128, 32),
+                                    (1, 4096)])
+def test_block_scales_layout(cuda_device, layout, rows, K):
+    """The relayout (its coalesced K-contiguous path and its generic path)
+    against the layout restated in numpy, byte for byte."""
+    kb = K // 32
+    g = torch.Generator(device="cuda").manual_seed(rows * 3 + kb)
+    base = torch.randint(0, 255, (rows, kb), generator=g, device="cuda").to(torch.uint8)
+    if layout == "k_contig":
+        s = base
+    elif layout == "k_contig_ragged":
+        s = base[:, : max(kb - 3, 1)]          # K/32 not a multiple of 16 (or of 4)
+    elif layout == "k_contig_padded_rows":
+        store = torch.zeros((rows, kb + 16), dtype=torch.uint8, device="cuda")
+        store[:, :kb] = base
+        s = store[:, :kb]                      # row stride kb + 16 (16-byte aligned)
+    elif layout == "m_contig":
+        s = base.T.contiguous().T
+    elif layout == "m_contig_rows_pad":
+        # the reference's storage: strides (1, rows rounded up to 256)
+        rows_pad = (rows + 255) // 256 * 256
+        store = torch.zeros((kb, rows_pad), dtype=torch.uint8, device="cuda")
+        store[:, :rows] = base.T
+        s = store[:, :rows].T
+    else:
+        store = torch.zeros((rows, 2 * kb + 1), dtype=torch.uint8, device="cuda")
+        store[:, : 2 * kb : 2] = base
+        s = store[:, : 2 * kb : 2]             # k stride 2, odd row stride
+    blocked = ops.block_scales(s)
+    torch.cuda.synchronize()
+    ops.check_status()
+    np.testing.assert_array_equal(blocked.data.cpu().numpy(), _blocked_ref(s.cpu().numpy()))
