@@ -19,9 +19,11 @@ Default (driver contract):  python bench.py [--gpus N] [--steps K] [--warmup W]
 Reference bench surface (kernels/gemm/intra_wave/<kind>/bench.py:133-164):
   python bench.py --kernel a16w16|a8w8|a4w4 [--K 8192] [--dtype fp16 bf16]
                   [--M 4096 --N 4096] [--rocprof] [--rotating-buffer-size 512]
+                  [--prepared]
   runs the correctness check against torch on the GPU and prints the TFLOPS
   table, or with --rocprof 1000 launches over rotating buffers for an external
-  profiler (ncu here).
+  profiler (ncu here). --prepared times prepared calls (ops.PreparedGemm,
+  planned once and then only launched), as scripts/benchmark_prepared.py does.
 """
 
 from __future__ import annotations
@@ -941,20 +943,28 @@ def reference_main(args, rank, world):
 
 
 # ------------------------------------------------- reference bench surface --
-def surface_call(kernel: str, dn: str, M: int, N: int, K: int, seed: int):
+def surface_call(kernel: str, dn: str, M: int, N: int, K: int, seed: int,
+                 prepared: bool = False):
     """A fresh input set of the reference bench's recipe and the call on it,
-    C preallocated (the rotating copies of a, b and c)."""
-    from gfx950_gluon_tutorials_b200 import a4w4, a8w8, a16w16
+    C preallocated (the rotating copies of a, b and c). `prepared`: the call as
+    an ops.PreparedGemm (the reference's --prepared route,
+    scripts/benchmark_prepared.py), planned once and then only launched."""
+    from gfx950_gluon_tutorials_b200 import a4w4, a8w8, a16w16, ops
     g = torch.Generator(device="cuda").manual_seed(1000 + seed)
     if kernel == "a16w16":
         dt = torch.float16 if dn == "fp16" else torch.bfloat16
         a = torch.randn((M, K), generator=g, device="cuda").to(dt)
         b = torch.randn((N, K), generator=g, device="cuda").to(dt).T
         c = torch.empty((M, N), device="cuda", dtype=dt)
+        if prepared:
+            return ops.prepare_gemm_f16(a, b.T, c)
         return lambda: a16w16.matmul(a, b, c)
     if kernel == "a8w8":
         a = (torch.rand((M, K), generator=g, device="cuda").half() - 0.5).to(torch.float8_e5m2)
         b = (torch.rand((N, K), generator=g, device="cuda").half().T - 0.5).to(torch.float8_e5m2)
+        if prepared:
+            return ops.prepare_gemm_f8(a, b.T, torch.empty((M, N), device="cuda",
+                                                           dtype=torch.float16))
         return lambda: a8w8.matmul(a, b)
     a = torch.randint(0, 256, (M, K // 2), generator=g, device="cuda", dtype=torch.uint8)
     b = torch.randint(0, 256, (N, K // 2), generator=g, device="cuda", dtype=torch.uint8)
@@ -963,6 +973,8 @@ def surface_call(kernel: str, dn: str, M: int, N: int, K: int, seed: int):
                        dtype=torch.uint8).T[:M]
     sb = torch.randint(124, 128, (K // 32, N), generator=g, device="cuda", dtype=torch.uint8).T
     c = torch.empty((M, N), device="cuda", dtype=torch.bfloat16)
+    if prepared:
+        return ops.prepare_gemm_mxf4(a, b, sa, sb, c)
     return lambda: a4w4.matmul(a, b, sa, sb, c)
 
 
@@ -1020,7 +1032,8 @@ def reference_surface_main(args):
                 # MB, launch i using copy i % copies
                 set_bytes = int((M + N) * K * elem) + M * N * 2
                 copies = max(1, args.rotating_buffer_size * 1024 * 1024 // set_bytes)
-                calls = [surface_call(args.kernel, dn, M, N, K, i) for i in range(copies)]
+                calls = [surface_call(args.kernel, dn, M, N, K, i, args.prepared)
+                         for i in range(copies)]
                 print(f"[{args.kernel}] M={M} N={N} K={K} dtype={dn}: rotating tensors: "
                       f"{copies} copies, {copies * set_bytes / 1024 ** 2:.0f} MB", flush=True)
                 calls[0]()
@@ -1032,6 +1045,8 @@ def reference_surface_main(args):
                 del calls
                 print(f"[{args.kernel}] M={M} N={N} K={K}: 1000 iterations done", flush=True)
                 continue
+            if args.prepared:
+                fn = surface_call(args.kernel, dn, M, N, K, 0, prepared=True)
             for _ in range(5):
                 fn()
             st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -1078,6 +1093,9 @@ def main():
     ap.add_argument("--M", type=int, default=4096)
     ap.add_argument("--N", type=int, default=4096)
     ap.add_argument("--rocprof", "--profile", dest="rocprof", action="store_true")
+    ap.add_argument("--prepared", action="store_true",
+                    help="time (or, with --rocprof, launch) prepared calls: planned once, "
+                         "then only launched (the reference's --prepared route)")
     ap.add_argument("--rotating-buffer-size", type=int, default=512)
     args = ap.parse_args()
     if args.kernel is not None:

@@ -49,6 +49,11 @@ SIGNATURES = {
                                        _c_i64, _c_i64, _vp, _c_i64, _vp, _c_int, _c_int, _c_int,
                                        _c_int, _c_int, _vp, _c_sz, _vp, _vp]),
     "b2g_gemm_grouped_workspace_bytes": (_c_sz, [_c_int, _c_int, _c_int, _c_int]),
+    "b2g_prepare_gemm": (_c_int, [_c_int, _vp, _c_i64, _vp, _c_i64, _vp, _c_i64, _c_i64, _vp,
+                                  _c_i64, _c_i64, _vp, _c_i64, _c_int, _c_int, _c_int, _c_int,
+                                  _vp, _c_sz, _vp, ctypes.POINTER(_vp)]),
+    "b2g_prepared_run": (_c_int, [_vp, _vp]),
+    "b2g_prepared_free": (None, [_vp]),
     "b2g_attention_fwd": (_c_int, [_vp, _vp, _vp, _vp, ctypes.POINTER(ctypes.c_int64), _c_int,
                                    _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
                                    ctypes.c_float, _vp, _vp, _vp]),

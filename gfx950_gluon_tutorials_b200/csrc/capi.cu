@@ -9,6 +9,7 @@
 #include <cstdint>
 #include <cstring>
 #include <mutex>
+#include <new>
 
 #include "b2g.h"
 #include "capi_internal.h"
@@ -410,8 +411,32 @@ int check_call(const GemmCall& c) {
   return B2G_OK;
 }
 
+// Everything one GEMM call launches, planned and with its tensor maps
+// encoded. Every entry point plans and launches once; a prepared call
+// (b2g_prepare_gemm) plans once and launches on every b2g_prepared_run.
+struct Launch {
+  int path;  // 0: the persistent kernel, 1: the small-M kernel
+  int kind, out_dtype, dev;
+  // persistent kernel
+  int cg, units;
+  bool relayout;  // the caller's (rows, K/32) scales are relaid first
+  const uint8_t* rl_sa;
+  int64_t rl_sa0, rl_sa1;
+  int rl_rows_a;
+  uint8_t* rl_dst_a;
+  const uint8_t* rl_sb;
+  int64_t rl_sb0, rl_sb1;
+  int rl_rows_b;
+  uint8_t* rl_dst_b;
+  int rl_kscales;
+  GemmParams prm;
+  // small-M kernel
+  int bn, blocks;
+  SkinnyParams sprm;
+};
+
 // C = A * B^T for M <= 128 with the swap-AB kernel (skinny_kernel.cuh).
-int run_skinny(const GemmCall& c, int sms) {
+int plan_skinny(const GemmCall& c, int sms, Launch* L) {
   const SkinnyGeom g = skinny_geometry(c.kind, c.M, c.N, c.K, sms);
   if (c.ws == nullptr || c.ws_bytes < g.total) return B2G_EWORKSPACE;
   if ((reinterpret_cast<uintptr_t>(c.ws) & 255u) != 0) return B2G_EALIGN;
@@ -438,25 +463,28 @@ int run_skinny(const GemmCall& c, int sms) {
   prm.splits = g.splits;
   prm.chunks_per_split = g.cps;
   prm.timeout_ns = static_cast<uint64_t>(g_opt.timeout_ms.load()) * 1000000ull;
-  const int blocks = g.tiles * g.splits;
-  switch (c.kind) {
-    case B2G_KIND_F16: return launch_skinny_bn<0>(prm, g.bn, blocks, c.out_dtype, c.stream);
-    case B2G_KIND_BF16: return launch_skinny_bn<1>(prm, g.bn, blocks, c.out_dtype, c.stream);
-    default: return launch_skinny_bn<2>(prm, g.bn, blocks, c.out_dtype, c.stream);
-  }
+  L->path = 1;
+  L->kind = c.kind;
+  L->out_dtype = c.out_dtype;
+  L->bn = g.bn;
+  L->blocks = g.tiles * g.splits;
+  L->sprm = prm;
+  return B2G_OK;
 }
 
 // `fixed`: a geometry the caller already planned (and sized its scratch by);
 // null plans here from the current options.
-int run_gemm(const GemmCall& c, const Geometry* fixed = nullptr) {
+int plan_gemm(const GemmCall& c, const Geometry* fixed, Launch* L) {
   int rc = check_call(c);
   if (rc != B2G_OK) return rc;
   int dev = -1;
   cudaGetDevice(&dev);
   const int sms = current_sms();
   if (sms <= 0) return B2G_ENODEVICE;
+  std::memset(L, 0, sizeof(*L));
+  L->dev = dev;
   if (fixed == nullptr && c.groups == nullptr && use_skinny(c.kind, c.M, c.N, sms))
-    return run_skinny(c, sms);
+    return plan_skinny(c, sms, L);
   const int b_rows = c.groups != nullptr ? c.n_groups * c.N : c.N;
   const Geometry g = fixed != nullptr
                          ? *fixed
@@ -465,8 +493,7 @@ int run_gemm(const GemmCall& c, const Geometry* fixed = nullptr) {
   if (c.ws != nullptr && (reinterpret_cast<uintptr_t>(c.ws) & 255u) != 0) return B2G_EALIGN;
   uint8_t* ws = static_cast<uint8_t*>(c.ws);
 
-  GemmParams prm;
-  std::memset(&prm, 0, sizeof(prm));
+  GemmParams& prm = L->prm;
   bool relayout = false;
   const int64_t eb = storage_elem_bytes(c.kind);
   const uint64_t rb = static_cast<uint64_t>(row_bytes(c.kind, c.K));
@@ -496,11 +523,17 @@ int run_gemm(const GemmCall& c, const Geometry* fixed = nullptr) {
     if (!aligned16(sfa) || !aligned16(sfb)) return B2G_EALIGN;
     if (!a_blocked || !b_blocked) {
       relayout = true;
-      const cudaError_t e = launch_sf_relayout(
-          a_blocked ? nullptr : c.sfa, c.sfa_s0, c.sfa_s1, c.M, ws + g.sfa_off,
-          b_blocked ? nullptr : c.sfb, c.sfb_s0, c.sfb_s1, b_rows, ws + g.sfb_off, c.K / 32,
-          c.stream);
-      if (e != cudaSuccess) return static_cast<int>(e);
+      L->rl_sa = a_blocked ? nullptr : c.sfa;
+      L->rl_sa0 = c.sfa_s0;
+      L->rl_sa1 = c.sfa_s1;
+      L->rl_rows_a = c.M;
+      L->rl_dst_a = ws + g.sfa_off;
+      L->rl_sb = b_blocked ? nullptr : c.sfb;
+      L->rl_sb0 = c.sfb_s0;
+      L->rl_sb1 = c.sfb_s1;
+      L->rl_rows_b = b_rows;
+      L->rl_dst_b = ws + g.sfb_off;
+      L->rl_kscales = c.K / 32;
     }
     const uint32_t gwords = static_cast<uint32_t>(c.kind == B2G_KIND_MXFP4 ? 256 : 128);
     const uint64_t row_words = static_cast<uint64_t>(g.sf_groups) * 128;
@@ -534,7 +567,37 @@ int run_gemm(const GemmCall& c, const Geometry* fixed = nullptr) {
   prm.group_rows = c.N;
   prm.timeout_ns = static_cast<uint64_t>(g_opt.timeout_ms.load()) * 1000000ull;
   prm.k_chunks = static_cast<int32_t>((rb + 127) / 128);
-  return dispatch(c.kind, g.cg, prm, g.launched, c.out_dtype, relayout, c.stream);
+  L->path = 0;
+  L->kind = c.kind;
+  L->out_dtype = c.out_dtype;
+  L->cg = g.cg;
+  L->units = g.launched;
+  L->relayout = relayout;
+  return B2G_OK;
+}
+
+int launch_planned(const Launch& L, cudaStream_t stream) {
+  if (L.path == 1) {
+    switch (L.kind) {
+      case B2G_KIND_F16: return launch_skinny_bn<0>(L.sprm, L.bn, L.blocks, L.out_dtype, stream);
+      case B2G_KIND_BF16: return launch_skinny_bn<1>(L.sprm, L.bn, L.blocks, L.out_dtype, stream);
+      default: return launch_skinny_bn<2>(L.sprm, L.bn, L.blocks, L.out_dtype, stream);
+    }
+  }
+  if (L.relayout) {
+    const cudaError_t e =
+        launch_sf_relayout(L.rl_sa, L.rl_sa0, L.rl_sa1, L.rl_rows_a, L.rl_dst_a, L.rl_sb,
+                           L.rl_sb0, L.rl_sb1, L.rl_rows_b, L.rl_dst_b, L.rl_kscales, stream);
+    if (e != cudaSuccess) return static_cast<int>(e);
+  }
+  return dispatch(L.kind, L.cg, L.prm, L.units, L.out_dtype, L.relayout, stream);
+}
+
+int run_gemm(const GemmCall& c, const Geometry* fixed = nullptr) {
+  Launch L;
+  const int rc = plan_gemm(c, fixed, &L);
+  if (rc != B2G_OK) return rc;
+  return launch_planned(L, c.stream);
 }
 
 }  // namespace
@@ -582,6 +645,11 @@ PFN_cuTensorMapEncodeTiled_v12000 tma_encoder() { return tensor_map_encoder(); }
 uint64_t wait_timeout_ns() { return static_cast<uint64_t>(g_opt.timeout_ms.load()) * 1000000ull; }
 
 }  // namespace b2g
+
+// The opaque handle of a prepared call: the planned launch itself.
+struct b2g_prepared {
+  Launch launch;
+};
 
 extern "C" {
 
@@ -711,6 +779,42 @@ size_t b2g_gemm_grouped_workspace_bytes(int M, int N, int K, int groups) {
   if (sms <= 0) return 0;
   return geometry(B2G_KIND_MXFP4, M, N, K, sms, pair_capacity(dev, sms), groups * N).total;
 }
+
+int b2g_prepare_gemm(int kind, const void* A, int64_t lda, const void* B, int64_t ldb,
+                     const uint8_t* sfa, int64_t sfa_s0, int64_t sfa_s1, const uint8_t* sfb,
+                     int64_t sfb_s0, int64_t sfb_s1, void* C, int64_t ldc, int M, int N, int K,
+                     int out_dtype, void* workspace, size_t workspace_bytes, int* status,
+                     b2g_prepared** out) {
+  if (out == nullptr) return B2G_EINVAL;
+  *out = nullptr;
+  if (kind < B2G_KIND_F16 || kind > B2G_KIND_MXFP4) return B2G_EINVAL;
+  if (!is_scaled(kind) && (sfa != nullptr || sfb != nullptr)) return B2G_EINVAL;
+  GemmCall c{};
+  c.kind = kind;
+  c.A = A; c.lda = lda; c.B = B; c.ldb = ldb;
+  c.sfa = sfa; c.sfa_s0 = sfa_s0; c.sfa_s1 = sfa_s1;
+  c.sfb = sfb; c.sfb_s0 = sfb_s0; c.sfb_s1 = sfb_s1;
+  c.C = C; c.ldc = ldc; c.M = M; c.N = N; c.K = K; c.out_dtype = out_dtype;
+  c.ws = workspace; c.ws_bytes = workspace_bytes; c.status = status;
+  auto* p = new (std::nothrow) b2g_prepared;
+  if (p == nullptr) return B2G_ECAPACITY;
+  const int rc = plan_gemm(c, nullptr, &p->launch);
+  if (rc != B2G_OK) {
+    delete p;
+    return rc;
+  }
+  *out = p;
+  return B2G_OK;
+}
+
+int b2g_prepared_run(const b2g_prepared* prepared, void* stream) {
+  if (prepared == nullptr) return B2G_EINVAL;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev != prepared->launch.dev) return B2G_ENODEVICE;
+  return launch_planned(prepared->launch, static_cast<cudaStream_t>(stream));
+}
+
+void b2g_prepared_free(b2g_prepared* prepared) { delete prepared; }
 
 int b2g_quant_mxfp4(const float* src, int64_t ld, int rows, int K, uint8_t* q, int64_t ldq,
                     uint8_t* scales, int64_t sc_s0, int64_t sc_s1, void* stream) {

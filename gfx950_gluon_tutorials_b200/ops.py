@@ -382,8 +382,131 @@ def plan_items(kind: int, M: int, N: int, K: int, unit: int, num_sms: int = 148)
     return [tuple(buf[11 * i:11 * i + 11]) for i in range(n)]
 
 
+class PreparedGemm:
+    """One GEMM call planned once and launched with nothing but the launch.
+
+    The counterpart of the reference's PreparedKernel (scripts/prepared_kernel.py:
+    76-138), which binds a launch's arguments once so that back-to-back calls pay
+    no launcher overhead (scripts/benchmark_prepared.py:255-260). Preparation
+    checks the operands, fixes the schedule under the current options and encodes
+    every tensor map (b2g_prepare_gemm); each call then launches on the current
+    stream (b2g_prepared_run) and returns C. The operands, scales and C stay
+    referenced: their contents may change between calls, their storage may not.
+    The call owns its workspace, so it can run on any stream, but two calls of
+    the same object must not overlap on the GPU. Build one with prepare_gemm_f16,
+    prepare_gemm_f8 or prepare_gemm_mxf4."""
+
+    def __init__(self, kind: int, a_: torch.Tensor, b_: torch.Tensor, sa: tuple, sb: tuple,
+                 c: torch.Tensor, M: int, N: int, K: int, keep: tuple):
+        dev = c.device
+        self.device, self.c = dev, c
+        self._keep = (a_, b_, c) + keep
+        # a zeroed workspace of its own (its flag words must read zero at rest)
+        self._ws = torch.zeros(max(lib().b2g_gemm_workspace_bytes(kind, M, N, K), 256),
+                               dtype=torch.uint8, device=dev)
+        self._h = ctypes.c_void_p()
+        rc = lib().b2g_prepare_gemm(kind, a_.data_ptr(), a_.stride(0), b_.data_ptr(),
+                                    b_.stride(0), *sa, *sb, c.data_ptr(), c.stride(0), M, N, K,
+                                    _OUT_DT[c.dtype], self._ws.data_ptr(), self._ws.numel(),
+                                    status_tensor(dev).data_ptr(), ctypes.byref(self._h))
+        check(rc, "b2g_prepare_gemm")
+
+    def __call__(self) -> torch.Tensor:
+        if not self._h:
+            raise B2GError(_lib.EINVAL, "prepared GEMM already closed")
+        check(lib().b2g_prepared_run(self._h, _stream_handle(self.device)), "b2g_prepared_run")
+        return self.c
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().b2g_prepared_free(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # interpreter shutdown: the library may be gone
+            pass
+
+
+def _in_place(t: torch.Tensor, name: str) -> torch.Tensor:
+    """The operand itself when the kernel can read it where it lies (a prepared
+    call keeps reading that storage, so a padded copy would go stale)."""
+    if _k_major(t) is not t:
+        raise ValueError(f"a prepared GEMM reads {name} in place: give it K-contiguous with "
+                         "16-byte aligned base and rows")
+    return t
+
+
+def _prepared_c(c: torch.Tensor | None, M: int, N: int, dtype: torch.dtype, dev) -> torch.Tensor:
+    c = _out(c, M, N, dtype, dev)
+    if _c_view(c)[1]:
+        raise ValueError("a prepared GEMM stores straight into C: give a C with unit column "
+                         "stride and 16-byte aligned rows")
+    return c
+
+
+def prepare_gemm_f16(a: torch.Tensor, b_t: torch.Tensor, c: torch.Tensor | None = None,
+                     out_dtype: torch.dtype | None = None) -> PreparedGemm:
+    """gemm_f16(a, b_t, c) as a PreparedGemm (same operand rules)."""
+    dev = _require_cuda(a, b_t)
+    if a.dtype not in (torch.float16, torch.bfloat16) or b_t.dtype != a.dtype:
+        raise ValueError(f"a16w16 takes two fp16 or two bf16 operands, got {a.dtype}, {b_t.dtype}")
+    M, K = a.shape
+    N, K2 = b_t.shape
+    if K != K2:
+        raise ValueError("Incompatible dimensions")
+    c = _prepared_c(c, M, N, out_dtype or (c.dtype if c is not None else a.dtype), dev)
+    kind = _lib.KIND_F16 if a.dtype == torch.float16 else _lib.KIND_BF16
+    return PreparedGemm(kind, _in_place(a, "a"), _in_place(b_t, "b_t"), (None, 0, 0),
+                        (None, 0, 0), c, M, N, K, ())
+
+
+def prepare_gemm_f8(a: torch.Tensor, b_t: torch.Tensor, c: torch.Tensor | None = None,
+                    a_scales=None, b_scales=None,
+                    out_dtype: torch.dtype = torch.float16) -> PreparedGemm:
+    """gemm_f8(a, b_t, c, a_scales, b_scales) as a PreparedGemm (same operand rules)."""
+    dev = _require_cuda(a, b_t)
+    for t in (a, b_t):
+        if t.dtype not in (torch.float8_e5m2, torch.uint8):
+            raise ValueError(f"a8w8 takes float8_e5m2 (or raw uint8) operands, got {t.dtype}")
+    if (a_scales is None) != (b_scales is None):
+        raise ValueError("give both scale tensors or neither")
+    M, K = a.shape
+    N, K2 = b_t.shape
+    if K != K2:
+        raise ValueError("Incompatible dimensions")
+    c = _prepared_c(c, M, N, c.dtype if c is not None else out_dtype, dev)
+    scaled = a_scales is not None
+    sa = _scale_args(a_scales, M, K, "a_scales") if scaled else (None, 0, 0)
+    sb = _scale_args(b_scales, N, K, "b_scales") if scaled else (None, 0, 0)
+    kind = _lib.KIND_MXE5M2 if scaled else _lib.KIND_E5M2
+    return PreparedGemm(kind, _in_place(_as_bytes(a), "a"), _in_place(_as_bytes(b_t), "b_t"), sa,
+                        sb, c, M, N, K, (a_scales, b_scales))
+
+
+def prepare_gemm_mxf4(a: torch.Tensor, b_t: torch.Tensor, a_scales, b_scales,
+                      c: torch.Tensor | None = None,
+                      out_dtype: torch.dtype = torch.bfloat16) -> PreparedGemm:
+    """gemm_mxf4(a, b_t, a_scales, b_scales, c) as a PreparedGemm (same operand rules)."""
+    dev = _require_cuda(a, b_t)
+    if a.dtype != torch.uint8 or b_t.dtype != torch.uint8:
+        raise ValueError("a4w4 operands are packed uint8")
+    M, Kp = a.shape
+    N, Kp2 = b_t.shape
+    if Kp != Kp2:
+        raise ValueError("Incompatible dimensions")
+    K = 2 * Kp
+    sa = _scale_args(a_scales, M, K, "a_scales")
+    sb = _scale_args(b_scales, N, K, "b_scales")
+    c = _prepared_c(c, M, N, c.dtype if c is not None else out_dtype, dev)
+    return PreparedGemm(_lib.KIND_MXFP4, _in_place(a, "a"), _in_place(b_t, "b_t"), sa, sb, c,
+                        M, N, K, (a_scales, b_scales))
+
+
 __all__ = [
     "B2GError", "BlockedScales", "block_scales", "gemm_f16", "gemm_f8", "gemm_mxf4",
     "quantize_mxfp4", "quantize_mxe5m2",
     "cast_e5m2", "workspace", "status_tensor", "check_status", "plan", "plan_items",
+    "PreparedGemm", "prepare_gemm_f16", "prepare_gemm_f8", "prepare_gemm_mxf4",
 ]

@@ -182,6 +182,30 @@ B2G_API int b2g_gemm_mxf4_grouped(const uint8_t* A, int64_t lda, const uint8_t* 
                                   size_t workspace_bytes, int* status, void* stream);
 B2G_API size_t b2g_gemm_grouped_workspace_bytes(int M, int N, int K, int groups);
 
+/* Prepared calls. Replaces the reference's PreparedKernel
+ * (scripts/prepared_kernel.py:76-138: create() binds a launch's arguments once,
+ * __call__ enters the compiled launcher directly), used by its kernel-only
+ * timing (scripts/benchmark_prepared.py:255-260) to take launch overhead out of
+ * back-to-back calls. b2g_prepare_gemm checks the arguments, plans the schedule
+ * and encodes every tensor map of one GEMM call (the arguments of
+ * b2g_gemm_f16 / _f8 / _mxf4, the operand kind given by `kind`; scales null for
+ * the unscaled kinds, both set for the scaled ones); each b2g_prepared_run then
+ * launches that call on `stream` with no further host work than the launch
+ * itself. The plan keeps the pointers, the workspace, the status word and the
+ * b2g_set_option values of the moment it was made: the buffers must stay
+ * allocated (their contents may change between runs), and calls that share the
+ * workspace must not overlap on the GPU. Runs must be made with the device
+ * current that was current at preparation (else B2G_ENODEVICE). Free the
+ * handle with b2g_prepared_free; *out is null when preparation fails. */
+typedef struct b2g_prepared b2g_prepared;
+B2G_API int b2g_prepare_gemm(int kind, const void* A, int64_t lda, const void* B, int64_t ldb,
+                             const uint8_t* sfa, int64_t sfa_s0, int64_t sfa_s1,
+                             const uint8_t* sfb, int64_t sfb_s0, int64_t sfb_s1, void* C,
+                             int64_t ldc, int M, int N, int K, int out_dtype, void* workspace,
+                             size_t workspace_bytes, int* status, b2g_prepared** out);
+B2G_API int b2g_prepared_run(const b2g_prepared* prepared, void* stream);
+B2G_API void b2g_prepared_free(b2g_prepared* prepared);
+
 /* Attention forward, non-causal, with grouped-query heads:
  *   O[b, h] = softmax(Q[b, h] K[b, g]^T * sm_scale) V[b, g],  g = h / (heads_q / heads_k)
  * Replaces run_gluon_attention (kernels/attention/fmha_v4.py:761-790) and the

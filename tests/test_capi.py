@@ -111,3 +111,25 @@ def test_options_roundtrip():
     assert _lib.lib().b2g_set_option(999, 1) == _lib.EINVAL
     assert _lib.get_option(_lib.OPT_SKINNY_MAX_M) == 128
     assert _lib.lib().b2g_set_option(_lib.OPT_SKINNY_MAX_M, 129) == _lib.EINVAL
+
+
+def test_prepare_gemm_argument_errors():
+    """Preparation checks the same arguments as the direct entry points before
+    touching a device, leaves the handle null on failure, and the run and free
+    entry points accept a null handle."""
+    lib = _lib.lib()
+    out = ctypes.c_void_p(12345)
+
+    def prep(kind=_lib.KIND_F16, A=16, sfa=None, sfb=None, K=64, outp=ctypes.byref(out)):
+        return lib.b2g_prepare_gemm(kind, A, 64, 16, 64, sfa, 1, 64, sfb, 1, 64, 16, 64, 64, 64,
+                                    K, 0, None, 0, None, outp)
+
+    assert prep(outp=None) == _lib.EINVAL
+    assert prep(kind=9) == _lib.EINVAL and out.value is None
+    assert prep(sfa=16, sfb=16) == _lib.EINVAL          # scales on an unscaled kind
+    assert prep(kind=_lib.KIND_MXFP4) == _lib.EINVAL     # scaled kind without scales
+    assert prep(A=24) == _lib.EALIGN
+    assert prep(kind=_lib.KIND_MXE5M2, sfa=16, sfb=16, K=48) == _lib.ESHAPE
+    assert out.value is None
+    assert lib.b2g_prepared_run(None, None) == _lib.EINVAL
+    lib.b2g_prepared_free(None)
