@@ -127,3 +127,33 @@ def test_prepared_calls_take_less_host_time(cuda_device):
     prepared = min(host_us(p) for _ in range(3))
     ops.check_status()
     assert prepared < direct, (prepared, direct)
+
+
+def test_calls_replay_from_a_cuda_graph(cuda_device):
+    """Direct and prepared calls captured in a CUDA graph (the launches carry
+    programmatic stream serialization) replay to the same bits as eager calls,
+    and a replay reads the inputs' current contents."""
+    a, b = _f16(1024, 2048, 4096, torch.float16, 11)
+    g = torch.Generator(device="cuda").manual_seed(12)
+    qa, sa = ops.quantize_mxfp4(torch.randn((512, 2048), generator=g, device="cuda"))
+    qb, sb = ops.quantize_mxfp4(torch.randn((768, 2048), generator=g, device="cuda"))
+    c1 = torch.empty((1024, 2048), dtype=torch.float16, device="cuda")
+    c2 = torch.empty((512, 768), dtype=torch.bfloat16, device="cuda")
+    p = ops.prepare_gemm_mxf4(qa, qb, sa, sb, c2)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):           # warm up on the capture stream (its workspace)
+        ops.gemm_f16(a, b, c1)
+        p()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        ops.gemm_f16(a, b, c1)
+        p()
+    a.mul_(0.5)
+    graph.replay()
+    torch.cuda.synchronize()
+    ops.check_status()
+    assert torch.equal(c1, ops.gemm_f16(a, b))
+    assert torch.equal(c2, ops.gemm_mxf4(qa, qb, sa, sb))
