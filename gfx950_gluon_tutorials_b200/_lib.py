@@ -26,7 +26,7 @@ SITE_EMPTY, SITE_FULL, SITE_ACC_EMPTY, SITE_ACC_FULL, SITE_OVERLAP, SITE_FLAG = 
 SITE_SCALES = 7
 OPT_PAIR, OPT_SK_MODE, OPT_GROUP_M, OPT_MIN_SK_ITERS, OPT_TIMEOUT_MS = 1, 2, 3, 4, 5
 OPT_INJECT_FLAG_TIMEOUT, OPT_MAX_UNITS, OPT_L2_PREFETCH, OPT_SKINNY_MAX_M = 6, 7, 8, 9
-OPT_SKINNY_SPLITS = 10
+OPT_SKINNY_SPLITS, OPT_SERPENTINE = 10, 11
 NOALLOC_SCRATCH_BYTES = 32 << 20
 
 _c_int, _c_i64, _c_sz, _vp = ctypes.c_int, ctypes.c_int64, ctypes.c_size_t, ctypes.c_void_p

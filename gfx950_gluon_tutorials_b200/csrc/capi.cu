@@ -38,7 +38,10 @@ namespace {
 struct Options {
   std::atomic<int64_t> pair{1};          // cta_group::2 CTA pairs
   std::atomic<int64_t> sk_mode{3};       // see make_plan
-  std::atomic<int64_t> group_m{1};
+  // 0: by kind. FP16/BF16 take 16 (whole column strips at 4096 x 4096: with
+  // the serpentine K order 195.0 against 197.6 us row-major), the 8-bit and
+  // 4-bit kinds 1 (row-major; 16 measured 0.1-0.5 us slower).
+  std::atomic<int64_t> group_m{0};
   // a split piece must span 16 stages: the fixed cost of publishing and adding
   // a partial tile (~13 us at 4096 x 4096) must stay below the half tile it saves
   std::atomic<int64_t> min_sk_iters{16};
@@ -48,6 +51,7 @@ struct Options {
   std::atomic<int64_t> prefetch{0};      // k-iterations pulled into L2 ahead of the ring
   std::atomic<int64_t> skinny_max_m{128};  // swap-AB kernel up to this M (0 = never)
   std::atomic<int64_t> skinny_splits{0};   // K splits per tile for it (0 = automatic)
+  std::atomic<int64_t> serpentine{1};      // odd waves walk K backwards
 };
 Options g_opt;
 
@@ -168,9 +172,12 @@ Geometry geometry(int kind, int M, int N, int K, int sms, int pair_cap = 0, int 
   const int tiles_n = (N + 255) / 256;
   const int k_chunks = static_cast<int>((row_bytes(kind, K) + 127) / 128);
   const int k_iters = (k_chunks + kKChunks - 1) / kKChunks;
-  g.plan = make_plan(tiles_m, tiles_n, k_iters, units, static_cast<int>(g_opt.group_m.load()),
+  int group_m = static_cast<int>(g_opt.group_m.load());
+  if (group_m == 0) group_m = (kind == B2G_KIND_F16 || kind == B2G_KIND_BF16) ? 16 : 1;
+  g.plan = make_plan(tiles_m, tiles_n, k_iters, units, group_m,
                      static_cast<int>(g_opt.sk_mode.load()),
                      static_cast<int>(g_opt.min_sk_iters.load()));
+  g.plan.serpentine = g_opt.serpentine.load() != 0 ? 1 : 0;
   g.launched = std::min(units, std::max(g.plan.dp_tiles, g.plan.sk_units));
   if (g.launched < 1) g.launched = 1;
   // Every workspace starts with the same fixed-size flag region (every unit
@@ -877,7 +884,7 @@ int b2g_set_option(int key, int64_t value) {
       g_opt.sk_mode.store(value);
       return B2G_OK;
     case B2G_OPT_GROUP_M:
-      if (value < 1 || value > 64) return B2G_EINVAL;
+      if (value < 0 || value > 64) return B2G_EINVAL;
       g_opt.group_m.store(value);
       return B2G_OK;
     case B2G_OPT_MIN_SK_ITERS:
@@ -905,6 +912,10 @@ int b2g_set_option(int key, int64_t value) {
       if (value < 0 || value > 64) return B2G_EINVAL;
       g_opt.skinny_splits.store(value);
       return B2G_OK;
+    case B2G_OPT_SERPENTINE:
+      if (value < 0 || value > 1) return B2G_EINVAL;
+      g_opt.serpentine.store(value);
+      return B2G_OK;
     default: return B2G_EINVAL;
   }
 }
@@ -921,6 +932,7 @@ int64_t b2g_get_option(int key) {
     case B2G_OPT_L2_PREFETCH: return g_opt.prefetch.load();
     case B2G_OPT_SKINNY_MAX_M: return g_opt.skinny_max_m.load();
     case B2G_OPT_SKINNY_SPLITS: return g_opt.skinny_splits.load();
+    case B2G_OPT_SERPENTINE: return g_opt.serpentine.load();
     default: return -1;
   }
 }

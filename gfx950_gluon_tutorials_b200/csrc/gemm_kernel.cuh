@@ -481,7 +481,8 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
         // scales of B: the tile's first (or, for the second half, second)
         // 128-row block comes first in the box
         const int32_t sfb_row = (b_base >> 7) + w.tn * 2 + (half ? w.nh : 0);
-        for (int32_t k = w.k_begin; k < w.k_end; ++k, ++it) {
+        for (int32_t kk = w.k_begin; kk < w.k_end; ++kk, ++it) {
+          const int32_t k = w.k_desc ? w.k_end - 1 - (kk - w.k_begin) : kk;
           const uint32_t s = it % STAGES, ph = (it / STAGES) & 1u;
           if (p.prefetch > 0) prefetch_one();
           if (!wait_phase_fast<false>(empty_bar(s), ph ^ 1u, abort_flag, p, B2G_SITE_EMPTY)) {
@@ -568,7 +569,8 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + b * SP::kAccStride;
         const bool half = w.nh >= 0;  // N = 128 instructions on the first 64 B rows per CTA
-        for (int32_t k = w.k_begin; k < w.k_end; ++k, ++it) {
+        for (int32_t kk = w.k_begin; kk < w.k_end; ++kk, ++it) {
+          const int32_t k = w.k_desc ? w.k_end - 1 - (kk - w.k_begin) : kk;
           const uint32_t s = it % STAGES, ph = (it / STAGES) & 1u;
           if (!wait_phase_fast<false>(full_bar(s), ph, abort_flag, p, B2G_SITE_FULL)) {
             alive = false;
@@ -599,7 +601,7 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
             // +32 bytes of K per MMA inside the 128-byte swizzled row
             const uint64_t ad = adesc + 2u * j;
             const uint64_t bd = bdesc + 2u * j;
-            const uint32_t acc = (k > w.k_begin || c > 0 || j > 0) ? 1u : 0u;
+            const uint32_t acc = (kk > w.k_begin || c > 0 || j > 0) ? 1u : 0u;
             if constexpr (KIND == kKindF16 || KIND == kKindBF16) {
               const uint32_t id = make_idesc<KIND, CG>(0);
               mma_f16<CG>(d_tmem, ad, bd, half ? idesc_half(id) : id, acc);
@@ -647,7 +649,8 @@ __global__ void __launch_bounds__((SmemPlan<KIND, CG, STAGES>::kThreads), 1)
         WorkItem w;
         bool alive = true;
         while (alive && cursor_next(p.plan, unit, cur, w)) {
-          for (int32_t k = w.k_begin; k < w.k_end; ++k, ++it) {
+          for (int32_t kk = w.k_begin; kk < w.k_end; ++kk, ++it) {
+          const int32_t k = w.k_desc ? w.k_end - 1 - (kk - w.k_begin) : kk;
             const uint32_t s = it % STAGES, ph = (it / STAGES) & 1u;
             // this stage's scales are in shared memory ...
             if (!wait_phase_fast<false>(sffull_bar(s), ph, abort_flag, p, B2G_SITE_FULL)) {

@@ -278,7 +278,8 @@ B2G_API int b2g_cast_e5m2(const void* src, int src_dtype, int64_t n, uint8_t* ds
                                  the tiles are too short to split, run each as
                                  two half-width (N = 128) tiles if they fit;
                                  4: half-width tiles whenever they fit, else as 3 */
-#define B2G_OPT_GROUP_M 3     /* raster group height in tiles (default 1: row-major) */
+#define B2G_OPT_GROUP_M 3     /* raster group height in tiles (1: row-major); default 0
+                                 picks by kind: 16 for fp16 / bf16, 1 otherwise */
 #define B2G_OPT_MIN_SK_ITERS 4 /* minimum k-iterations (256-byte stages) per stream-K unit
                                   or split piece (default 16) */
 #define B2G_OPT_TIMEOUT_MS 5  /* bounded-wait deadline in ms (default 2000) */
@@ -294,6 +295,10 @@ B2G_API int b2g_cast_e5m2(const void* src, int src_dtype, int64_t n, uint8_t* ds
                                   128-row side, A's rows on its N side */
 #define B2G_OPT_SKINNY_SPLITS 10 /* K splits per 128-column tile in that kernel
                                     (default 0 = chosen from the SM count) */
+#define B2G_OPT_SERPENTINE 11 /* 1 (default): the data-parallel tiles of odd waves run
+                                 their K loop backwards, starting on the k-chunks the
+                                 previous wave read last (still in L2); 0: every
+                                 tile runs K forwards */
 
 B2G_API int b2g_set_option(int key, int64_t value);
 B2G_API int64_t b2g_get_option(int key);

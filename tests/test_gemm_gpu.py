@@ -54,14 +54,18 @@ def assert_close(c: np.ndarray, ref: np.ndarray, tol: float, ref_atol: bool = Tr
     dict(pair=1, sk=4, min_sk=4, units=0),   # leftover tiles as half-width tiles
     dict(pair=0, sk=4, min_sk=4, units=0),
     dict(pair=1, sk=4, min_sk=1, units=13),  # few units: halves fit only sometimes
-], ids=lambda d: f"pair{d['pair']}-sk{d['sk']}-min{d['min_sk']}-u{d['units']}")
+    dict(pair=1, sk=3, min_sk=4, units=3, serp=0),  # every tile walks K forwards
+    dict(pair=0, sk=1, min_sk=4, units=5, serp=0),
+], ids=lambda d: f"pair{d['pair']}-sk{d['sk']}-min{d['min_sk']}-u{d['units']}"
+                 + ("-fwd" if d.get("serp", 1) == 0 else ""))
 def sched(request, cuda_device):
     """Main-kernel schedule variants; the small-M swap-AB kernel is switched off
     so that these cases keep exercising the persistent kernel."""
     keys = {"pair": _lib.OPT_PAIR, "sk": _lib.OPT_SK_MODE, "min_sk": _lib.OPT_MIN_SK_ITERS,
-            "units": _lib.OPT_MAX_UNITS, "skinny": _lib.OPT_SKINNY_MAX_M}
+            "units": _lib.OPT_MAX_UNITS, "skinny": _lib.OPT_SKINNY_MAX_M,
+            "serp": _lib.OPT_SERPENTINE}
     old = {k: _lib.get_option(v) for k, v in keys.items()}
-    for k, v in dict(request.param, skinny=0).items():
+    for k, v in dict(dict(serp=1), **request.param, skinny=0).items():
         _lib.set_option(keys[k], v)
     yield request.param
     for k, v in old.items():
@@ -428,6 +432,31 @@ def test_a4w4_full_size_sampled_rows(cuda_device):
     ref = mx.gemm_mxfp4_ref(qa[rows].cpu().numpy(), qb.cpu().numpy(),
                             sa[rows].cpu().numpy(), sb.cpu().numpy())
     assert_close(as_f32(c[rows]), mx.bf16_bits_to_f32(ref), TOL_F8, ref_atol=False)
+
+
+def test_serpentine_k_order(cuda_device):
+    """Odd waves walking K backwards change only the order of the fp32 sums:
+    at 4096 x 4096 x 8192 (three full waves) FP16 stays within the tolerance of
+    the fp32 product either way, and MXFP4 with the reference's inputs (whose
+    products are multiples of 2^-8, summed exactly) is bit-identical."""
+    M = N = 4096
+    K = 8192
+    a = (torch.randn((M, K), device="cuda") / K ** 0.5).half()
+    b_t = (torch.randn((N, K), device="cuda") / K ** 0.5).half()
+    qa, qb, sa, sb = _reference_style_mxfp4(M, N, K, seed=77)
+    old = _lib.get_option(_lib.OPT_SERPENTINE)
+    try:
+        out = {}
+        for serp in (1, 0):
+            _lib.set_option(_lib.OPT_SERPENTINE, serp)
+            out[serp] = (ops.gemm_f16(a, b_t), ops.gemm_mxf4(qa, qb, sa, sb))
+        ops.check_status()
+    finally:
+        _lib.set_option(_lib.OPT_SERPENTINE, old)
+    full = a.float() @ b_t.float().T
+    for serp in (1, 0):
+        assert _gpu_normalised_err(out[serp][0], full) <= TOL_F16
+    assert torch.equal(out[1][1], out[0][1])
 
 
 def test_repeated_calls_are_deterministic(cuda_device):
