@@ -34,6 +34,8 @@
 // wave starts on the k-chunks of the panels the previous wave read last, which
 // are still in L2 (FP16 4096 x 4096 x 8192: 323 -> 251 MB read from DRAM per
 // launch). The fp32 sums of those tiles are taken in the opposite order.
+// Bit 1 extends the rule to the leftover items (split pieces, half tiles,
+// stream-K segments), which run as the wave after the data-parallel ones.
 // Pair rule (a tile split into two pieces): each piece reduces half of the
 // tile's columns. Piece s keeps columns [128 s, 128 s + 128): it publishes its
 // partial of the other half, raises its flag, then waits for its peer's flag
@@ -64,7 +66,8 @@ struct SkPlan {
   int32_t group_m;           // raster group height in tiles
   int32_t splits;            // split mode: k-chunks per leftover tile (0 = stream-K)
   int32_t half;              // 1: leftover tiles run as half-width items (units [0, sk_units))
-  int32_t serpentine;        // 1: data-parallel tiles of odd waves walk K backwards
+  int32_t serpentine;        // bit 0: data-parallel tiles of odd waves walk K backwards;
+                             // bit 1: so do the leftover items when their wave is odd
 };
 
 struct WorkItem {
@@ -196,12 +199,14 @@ B2G_HD bool cursor_next(const SkPlan& p, int32_t u, WorkCursor& c, WorkItem& w) 
     w.k_begin = 0;
     w.k_end = p.k_iters;
     w.role = kRoleFull;
-    w.k_desc = p.serpentine & (w.tile / p.units);
+    w.k_desc = p.serpentine & (w.tile / p.units) & 1;
     c.dp_next += p.units;
     tile_coords(p, w.tile, w.tm, w.tn);
     return true;
   }
   if (c.sk_pos >= c.sk_end) return false;
+  // the leftover items run as wave dp_tiles / units
+  w.k_desc = (p.serpentine >> 1) & (p.dp_tiles / p.units) & 1;
   if (p.half) {
     // half mode: units 2j, 2j + 1 take the two column halves of leftover tile j
     w.tile = p.dp_tiles + (u >> 1);
