@@ -38,10 +38,7 @@ namespace {
 struct Options {
   std::atomic<int64_t> pair{1};          // cta_group::2 CTA pairs
   std::atomic<int64_t> sk_mode{3};       // see make_plan
-  // 0: by kind. FP16/BF16 take 16 (whole column strips at 4096 x 4096: with
-  // the serpentine K order 195.0 against 197.6 us row-major), the 8-bit and
-  // 4-bit kinds 1 (row-major; 16 measured 0.1-0.5 us slower).
-  std::atomic<int64_t> group_m{0};
+  std::atomic<int64_t> group_m{0};       // 0: chosen from the operand sizes (auto_group_m)
   // a split piece must span 16 stages: the fixed cost of publishing and adding
   // a partial tile (~13 us at 4096 x 4096) must stay below the half tile it saves
   std::atomic<int64_t> min_sk_iters{16};
@@ -157,6 +154,31 @@ int64_t blocked_scale_bytes(int64_t rows, int64_t K) {
   return ((rows + 127) / 128) * ((K / 32 + 3) / 4) * 512;
 }
 
+// Raster group height when B2G_OPT_GROUP_M is 0, chosen so that the panels a
+// wave shares stay in the 126 MB L2 and each operand is read from DRAM as few
+// times as possible:
+//  - A and B together within 96 MiB: everything stays in L2; row-major;
+//  - A within 64 MiB: whole column strips (A stays, B is read once);
+//  - B within 64 MiB: row-major (B stays, A is read once);
+//  - neither: bands of tile rows whose A panels total about 32 MiB, walked
+//    column by column (B is read once per band).
+// Grouped GEMMs keep row-major: consecutive tile rows belong to one expert.
+// Measured (interleaved, one box): FP16 4096 x 4096 x 8192 193.4 us in column
+// strips against 196.4 us row-major, 3840^2 178.0 against 180.0; MXFP4
+// 16384 x 53248 x 16384 (2 MiB A panels) 6.46 ms row-major, 5.63 / 5.37 / 5.75
+// ms in bands of 8 / 16 / 32 tile rows; the 8- and 4-bit kinds at 4096^2, which
+// fit in L2, 0.1-0.5 us slower in column strips.
+int auto_group_m(int64_t rb, int M, int b_rows, int N, int cg, int tiles_m) {
+  constexpr double kMiB = 1024.0 * 1024.0;
+  const double a_bytes = static_cast<double>(M) * rb, b_bytes = static_cast<double>(b_rows) * rb;
+  if (b_rows != N || a_bytes + b_bytes <= 96 * kMiB) return 1;
+  if (a_bytes <= 64 * kMiB) return tiles_m;
+  if (b_bytes <= 64 * kMiB) return 1;
+  const double panel = 128.0 * cg * rb;
+  const int band = static_cast<int>(32 * kMiB / panel);
+  return std::max(1, std::min(band, tiles_m));
+}
+
 // `pair_cap`: how many CTA pairs the device can hold at once (0 = sms / 2).
 // `b_rows`: rows of B and its scales (N, or groups * N for a grouped GEMM).
 Geometry geometry(int kind, int M, int N, int K, int sms, int pair_cap = 0, int b_rows = 0) {
@@ -173,7 +195,7 @@ Geometry geometry(int kind, int M, int N, int K, int sms, int pair_cap = 0, int 
   const int k_chunks = static_cast<int>((row_bytes(kind, K) + 127) / 128);
   const int k_iters = (k_chunks + kKChunks - 1) / kKChunks;
   int group_m = static_cast<int>(g_opt.group_m.load());
-  if (group_m == 0) group_m = (kind == B2G_KIND_F16 || kind == B2G_KIND_BF16) ? 16 : 1;
+  if (group_m == 0) group_m = auto_group_m(row_bytes(kind, K), M, b_rows, N, g.cg, tiles_m);
   g.plan = make_plan(tiles_m, tiles_n, k_iters, units, group_m,
                      static_cast<int>(g_opt.sk_mode.load()),
                      static_cast<int>(g_opt.min_sk_iters.load()));

@@ -279,7 +279,10 @@ B2G_API int b2g_cast_e5m2(const void* src, int src_dtype, int64_t n, uint8_t* ds
                                  two half-width (N = 128) tiles if they fit;
                                  4: half-width tiles whenever they fit, else as 3 */
 #define B2G_OPT_GROUP_M 3     /* raster group height in tiles (1: row-major); default 0
-                                 picks by kind: 16 for fp16 / bf16, 1 otherwise */
+                                 picks it from the operand sizes: row-major when A and
+                                 B fit in L2 together or B alone does, whole column
+                                 strips when A alone does, else bands of tile rows
+                                 holding about 32 MiB of A */
 #define B2G_OPT_MIN_SK_ITERS 4 /* minimum k-iterations (256-byte stages) per stream-K unit
                                   or split piece (default 16) */
 #define B2G_OPT_TIMEOUT_MS 5  /* bounded-wait deadline in ms (default 2000) */

@@ -132,3 +132,17 @@ def test_half_mode_plans(half_mode):
     # 50 leftover tiles (2 x 50 > 74 units): k-splits instead
     p = ops.plan(_lib.KIND_F16, 256 * 11, 256 * 11, 8192, 148)   # 121 tiles = 74 + 47
     assert p["dp_tiles"] == 74 and p["half"] == 0 and p["splits"] >= 1
+
+
+@pytest.mark.parametrize("kind,M,N,K,expect", [
+    (_lib.KIND_F16, 4096, 4096, 8192, 16),      # A (64 MiB) stays in L2: column strips
+    (_lib.KIND_F16, 3840, 3840, 8192, 15),
+    (_lib.KIND_MXE5M2, 4096, 4096, 8192, 1),    # A and B fit in L2 together: row-major
+    (_lib.KIND_MXFP4, 4096, 4096, 8192, 1),
+    (_lib.KIND_MXFP4, 16384, 53248, 16384, 16),  # neither fits: bands of 16 x 2 MiB of A
+    (_lib.KIND_MXFP4, 16384, 13312, 16384, 16),
+    (_lib.KIND_MXFP4, 16384, 6656, 16384, 1),    # B (52 MiB) stays in L2: row-major
+])
+def test_automatic_raster_group(kind, M, N, K, expect):
+    assert _lib.get_option(_lib.OPT_GROUP_M) == 0
+    assert ops.plan(kind, M, N, K, 148)["group_m"] == expect
