@@ -459,6 +459,21 @@ def test_serpentine_k_order(cuda_device):
     assert torch.equal(out[1][1], out[0][1])
 
 
+def test_banded_raster_fp16_8192(cuda_device):
+    """A and B of 128 MiB each exceed L2, so the raster walks bands of 8 tile
+    rows (32 MiB of A) column by column, with odd waves walking K backwards:
+    the whole C against the fp32 GPU product."""
+    M = N = K = 8192
+    assert ops.plan(_lib.KIND_F16, M, N, K, torch.cuda.get_device_properties(0)
+                    .multi_processor_count)["group_m"] == 8
+    g = torch.Generator(device="cuda").manual_seed(88)
+    a = (torch.randn((M, K), generator=g, device="cuda") / K ** 0.5).half()
+    b_t = (torch.randn((N, K), generator=g, device="cuda") / K ** 0.5).half()
+    c = ops.gemm_f16(a, b_t)
+    ops.check_status()
+    assert _gpu_normalised_err(c, a.float() @ b_t.float().T) <= TOL_F16
+
+
 def test_repeated_calls_are_deterministic(cuda_device):
     """Stream-K reduces partials in a fixed order: identical inputs, identical bits."""
     old = _lib.get_option(_lib.OPT_MIN_SK_ITERS)
